@@ -1,0 +1,446 @@
+"""Benchmark of the tree-shared decode-attention step on B200.
+
+Workload (BASELINE headline, configs[1]): 128 requests, each with an 8192-token
+context: a shared 8128-token root then 128 private 64-token leaves (16,320
+physical / 1,048,576 logical KV positions); 32 query heads, 8 KV heads,
+head_dim 128; Q/K/V BF16 drawn N(0,1) from a seed (synthetic data, no dataset);
+one decode query per request; subset-DP ("cube") plan with the B200 cost model.
+
+One step = one decode-step attention: the segment kernels over every
+(job, KV head) plus the LSE merge, inputs resident in HBM.  Metric: physical-KV
+HBM throughput (physical KV bytes / step time, GB/s, higher is better); the
+step latency in microseconds is reported beside it.  The KV working set
+(66.8 MB) fits in the 126 MB L2, so a 512 MB buffer is overwritten between
+timed steps (L2 flush) outside the timed events.
+
+With ``--gpus N`` (launched by torchrun, one process per GPU) the 8 KV heads are
+sharded: rank r owns heads [r*8/N, (r+1)*8/N) with their query heads and that
+slice of the pools; the plan is identical on every rank; no collective runs
+inside attention.  Total work is fixed (strong scaling); the step time is the
+max over ranks.
+
+``--impl reference`` times the reference's CPU implementation of the path --
+the FP32 plan-driven oracle (restated under ``oracle/``), all host threads --
+on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "tree-attention-scheduling_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+from tree_attention import CostModel, KVTree, schedule  # noqa: E402
+from tree_attention import kernels  # noqa: E402
+from tree_attention import _lib  # noqa: E402
+
+METRIC = "tree-attn decode step µs & physical-KV HBM GB/s, 128req×8K ctx, 1–8 B200"
+NREQ, ROOT_LEN, LEAF_LEN = 128, 8128, 64
+HQ, HK, D = 32, 8, 128
+SEED = 101
+FLUSH_BYTES = 512 << 20
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def headline_tree():
+    return KVTree.synthetic([-1] + [0] * NREQ, [ROOT_LEN] + [LEAF_LEN] * NREQ, list(range(1, NREQ + 1)))
+
+
+def kv_bytes(tree, heads=HK):
+    return tree.storage_tokens * heads * D * 2 * 2
+
+
+def logical_flops(tree, q_heads=HQ):
+    return 4 * D * q_heads * sum(len(p) for p in tree.paths)
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data["hbm_gbs"], data["bf16_tflops"], "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the segment phase from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / "seg_headline_traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_step:"):
+            return int(line.split(":", 1)[1].strip())
+    return None
+
+
+# ---------------------------------------------------------------------------
+# inputs: every KV head (and its query heads) from its own generator, so the
+# data are identical whatever the number of shards.
+def make_inputs(tree, heads, device):
+    storage = tree.storage_tokens
+    G = HQ // HK
+    q = torch.empty(NREQ, len(heads) * G, D, dtype=torch.bfloat16, device=device)
+    kp = torch.empty(len(heads), storage, D, dtype=torch.bfloat16, device=device)
+    vp = torch.empty_like(kp)
+    for i, h in enumerate(heads):
+        g = torch.Generator(device=device).manual_seed(SEED * 1000 + h)
+        q[:, i * G:(i + 1) * G] = torch.randn(NREQ, G, D, generator=g, device=device).bfloat16()
+        kp[i] = torch.randn(storage, D, generator=g, device=device).bfloat16()
+        vp[i] = torch.randn(storage, D, generator=g, device=device).bfloat16()
+    return q, kp, vp
+
+
+class ClockSampler:
+    """NVML sampler of SM clock and clock-event reasons (read-only)."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index, period=0.005):
+        self.samples, self.reasons = [], 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # pragma: no cover - depends on the driver
+            self._nvml = None
+            self.error = repr(exc)
+        self.period = period
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self._nvml:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread:
+            self._stop.set()
+            self._thread.join()
+        names = sorted(n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle")
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples),
+                "source": "nvml" if self._nvml else "unavailable"}
+
+
+# ---------------------------------------------------------------------------
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N > 1 must be launched with torchrun (one process per GPU)")
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+class Step:
+    """One decode step of a prepared plan, split into segment and merge launches."""
+
+    def __init__(self, q, kp, vp, prepared):
+        self.q, self.kp, self.vp, self.p = q, kp, vp, prepared
+        self.lib = _lib.load()
+        L = prepared.layout
+        self.launches = (sum(1 for i, e in enumerate(L.small_class_end) if e > (L.small_class_end[i - 1] if i else 0))
+                         + (1 if L.num_tc_tasks else 0) + 1)
+
+    def segment(self):
+        p = self.p
+        rc = self.lib.ta_segment(p.layout, p.metadata.data_ptr(), self.q.data_ptr(), self.kp.data_ptr(),
+                                 self.vp.data_ptr(), self.kp.shape[1], self.q.shape[1], self.kp.shape[0], D,
+                                 _lib.DTYPE_BF16, p.part.data_ptr(), p.lse.data_ptr(), p.status.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream)
+        _lib.check(rc, "ta_segment")
+
+    def merge(self):
+        p = self.p
+        rc = self.lib.ta_merge(p.layout, p.metadata.data_ptr(), p.part.data_ptr(), p.lse.data_ptr(),
+                               p.out.data_ptr(), None, self.q.shape[1], self.kp.shape[0], D, _lib.DTYPE_BF16,
+                               p.status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        _lib.check(rc, "ta_merge")
+
+
+def capture(fn):
+    """Record fn's launches into a CUDA graph (after one eager warm call)."""
+    fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(graph, stream=stream):
+        fn()
+    torch.cuda.synchronize()
+    return graph
+
+
+def time_step(step, steps, warmup, flush, world, use_graph=True):
+    """Device time (µs) per step of the segment phase and the merge, L2 flushed between steps."""
+    if use_graph:
+        g_seg, g_merge = capture(step.segment), capture(step.merge)
+        seg, merge = g_seg.replay, g_merge.replay
+    else:
+        seg, merge = step.segment, step.merge
+    for _ in range(warmup):
+        flush.zero_()
+        seg()
+        merge()
+    barrier(world)
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for e0, e1, e2 in events:
+        flush.zero_()
+        e0.record()
+        seg()
+        e1.record()
+        merge()
+        e2.record()
+    barrier(world)
+    seg_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in events)
+    merge_ms = sum(e1.elapsed_time(e2) for _, e1, e2 in events)
+    return seg_ms * 1e3 / steps, merge_ms * 1e3 / steps
+
+
+def time_e2e(q_host, step, steps, warmup, flush, world):
+    """Public-API step with host buffers: H2D of the queries, attention_matrix, D2H of the output."""
+    out_host = torch.empty(step.p.out.shape, dtype=step.p.out.dtype, pin_memory=True)
+    q_dev = step.q
+
+    def one():
+        q_dev.copy_(q_host, non_blocking=True)
+        out = kernels.attention_matrix(q_dev, step.kp, step.vp, step.p)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(warmup):
+        flush.zero_()
+        one()
+    barrier(world)
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in pairs:
+        flush.zero_()
+        e0.record()
+        one()
+        e1.record()
+    barrier(world)
+    us = sum(a.elapsed_time(b) for a, b in pairs) * 1e3 / steps
+    return us, q_host.numel() * q_host.element_size(), out_host.numel() * out_host.element_size()
+
+
+def cpu_oracle_step_us(tree, plan, q, kp, vp, budget_s=10.0, max_steps=200):
+    """The FP32 plan-driven oracle on the host cores, repeated for about budget_s seconds."""
+    from oracle import attention as oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    qc = q.float().cpu()
+    kc = kp.float().cpu().permute(1, 0, 2).contiguous()
+    vc = vp.float().cpu().permute(1, 0, 2).contiguous()
+    oracle.segmented_attention(qc, kc, vc, plan.jobs)          # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_steps and (n == 0 or time.perf_counter() - t0 < budget_s):
+        oracle.segmented_attention(qc, kc, vc, plan.jobs)
+        n += 1
+    return (time.perf_counter() - t0) * 1e6 / n, n, threads
+
+
+def run_b200(args):
+    rank, world, local = setup_dist(args)
+    if HK % world:
+        raise SystemExit("the 8 KV heads must divide evenly over the GPUs")
+    heads = list(range(rank * HK // world, (rank + 1) * HK // world))
+    tree = headline_tree()
+    dev = torch.device("cuda", local)
+    q, kp, vp = make_inputs(tree, heads, dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    model = CostModel.b200()
+
+    results = {}
+    t0 = time.perf_counter()
+    plan = schedule(tree, HQ, HK, D, args.method, model)
+    plan_us = (time.perf_counter() - t0) * 1e6
+    t0 = time.perf_counter()
+    prepared = kernels.prepare(plan, q, num_kv_heads=len(heads))
+    torch.cuda.synchronize()
+    metadata_us = (time.perf_counter() - t0) * 1e6
+    step = Step(q, kp, vp, prepared)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    burn_end = time.perf_counter() + args.burn_s
+    while time.perf_counter() < burn_end:       # sustained load so the clock samples see the step
+        flush.zero_()
+        step.segment()
+        step.merge()
+    seg_us, merge_us = time_step(step, args.steps, args.warmup, flush, world)
+    clocks = sampler.stop()
+    kernels.check_status(prepared)
+    step_us_local = seg_us + merge_us
+    step_us = max_over_ranks(step_us_local, world)
+    seg_us_max = max_over_ranks(seg_us, world)
+
+    # other plans on the same kernels (same shards), for the speed-up columns
+    for method, m in (("request", CostModel()), ("fixed", model), ("greedy", model)):
+        if not args.all_plans and method != "request":
+            continue
+        pl = kernels.prepare(schedule(tree, HQ, HK, D, method, m), q, num_kv_heads=len(heads))
+        s, mg = time_step(Step(q, kp, vp, pl), max(3, args.steps // 2), args.warmup, flush, world)
+        results[method] = {"step_us": max_over_ranks(s + mg, world), "jobs": len(pl.jobs)}
+        del pl
+
+    q_host = q.cpu().pin_memory()
+    e2e_us, h2d, d2h = time_e2e(q_host, step, args.steps, args.warmup, flush, world)
+    e2e_us = max_over_ranks(e2e_us, world)
+    kernels.check_status(prepared)
+
+    total_bytes = kv_bytes(tree)                     # all ranks together
+    local_bytes = kv_bytes(tree, len(heads))
+    hbm_peak, tf_peak, peak_kind = peaks()
+    achieved = local_bytes / (seg_us * 1e-6) / 1e9
+    value = total_bytes / (step_us * 1e-6) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(step_us / 1e3, 6), "step_us": round(step_us, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) BF16 Q/K/V)",
+        "config": {"workload": "headline: 128 req x 8192 ctx, shared 8128-token root + 128 x 64-token leaves, "
+                               "HQ=32 HK=8 D=128, one decode query per request",
+                   "plan": args.method, "cost_model": "CostModel.b200()", "jobs": len(prepared.jobs),
+                   "physical_kv_bytes": total_bytes, "logical_kv_bytes": sum(len(p) for p in tree.paths) * HK * D * 4,
+                   "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                   "l2": "512 MB buffer overwritten between timed steps (KV set 66.8 MB < 126 MB L2)",
+                   "timing": "CUDA events per step around CUDA-graph replays of the segment and merge launches",
+                   "plan_us": round(plan_us, 1), "metadata_us": round(metadata_us, 1)},
+        "segment_us": round(seg_us_max, 3), "merge_us": round(max_over_ranks(merge_us, world), 3),
+        "e2e": {"value": round(total_bytes / (e2e_us * 1e-6) / 1e9, 2), "unit": "GB/s", "step_us": round(e2e_us, 3),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "kernels.attention_matrix with pinned host Q in / output out"},
+        "gpu_launches": step.launches * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": profile_traffic(),
+                     "kernel": "segment phase (all segment launches of one step)",
+                     "peak_source": f"{peak_kind} hbm_gbs",
+                     "tensor_tflops": round(logical_flops(tree, HQ * len(heads) // HK) / (seg_us * 1e-6) / 1e12, 1),
+                     "tensor_frac": round(logical_flops(tree, HQ * len(heads) // HK) / (seg_us * 1e-6) / 1e12 /
+                                          tf_peak, 4)},
+        "clocks": clocks,
+        "plans": results,
+    }
+    if "request" in results:
+        line["per_request_speedup"] = round(results["request"]["step_us"] / step_us, 3)
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu_us, n, threads = cpu_oracle_step_us(tree, plan, q, kp, vp, budget_s=args.cpu_budget_s)
+        line["cpu_baseline"] = {"value": round(total_bytes / (cpu_us * 1e-6) / 1e9, 4), "unit": "GB/s",
+                                "step_us": round(cpu_us, 1), "cores": threads, "kind": "port",
+                                "sample": f"{n} full headline steps of the FP32 plan-driven oracle "
+                                          f"(oracle/attention.py segmented_attention, same cube plan)"}
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_reference(args):
+    """The reference's CPU implementation of the path (FP32 oracle port), rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import attention as oracle
+    tree = headline_tree()
+    plan = schedule(tree, HQ, HK, D, args.method, CostModel.b200())
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(SEED)
+    q = torch.randn(NREQ, HQ, D, generator=g).bfloat16().float()
+    k = torch.randn(tree.storage_tokens, HK, D, generator=g).bfloat16().float()
+    v = torch.randn(tree.storage_tokens, HK, D, generator=g).bfloat16().float()
+    for _ in range(args.warmup):
+        oracle.segmented_attention(q, k, v, plan.jobs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.segmented_attention(q, k, v, plan.jobs)
+    us = (time.perf_counter() - t0) * 1e6 / args.steps
+    value = kv_bytes(tree) / (us * 1e-6) / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3), "step_us": round(us, 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) BF16-valued Q/K/V)",
+            "config": {"workload": "headline: 128 req x 8192 ctx, shared 8128-token root + 128 x 64-token leaves, "
+                                   "HQ=32 HK=8 D=128", "plan": args.method, "cost_model": "CostModel.b200()"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} full headline steps of the FP32 plan-driven oracle"},
+            "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--method", default="cube", choices=["request", "fixed", "greedy", "cube"])
+    ap.add_argument("--all-plans", action="store_true", help="also time the fixed and greedy plans")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=10.0)
+    ap.add_argument("--burn-s", type=float, default=1.0, help="sustained untimed load before timing (clocks)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,137 @@
+/*
+ * tree_attn.h -- C ABI of the B200 (sm_100a) tree-shared decode-attention kernels.
+ *
+ * The reference (Gxj230958/tree-attention-scheduling) drives its two Triton
+ * kernels from Python (src/tree_attention/kernels.py).  These entry points are
+ * the boundary those launches map to; every argument is a plain pointer or
+ * integer, no framework types.  Device pointers are CUDA global-memory
+ * addresses on the current device; `stream` is a cudaStream_t (NULL = legacy
+ * default stream).  No entry point synchronises the stream or allocates
+ * memory, so all of them can be recorded into a CUDA graph.
+ *
+ * Layouts (all row-major, contiguous):
+ *   q      [num_requests, num_q_heads, head_dim]            bf16 or f16
+ *   kpool  [num_kv_heads, pool_tokens, head_dim]             same dtype as q
+ *   vpool  [num_kv_heads, pool_tokens, head_dim]             same dtype as q
+ *   part   [num_kv_heads, num_partials * G, head_dim]        f32 scratch
+ *   lse    [num_kv_heads, num_partials * G]                  f32 scratch
+ *   out    [num_requests, num_q_heads, head_dim]             dtype of q
+ * with G = num_q_heads / num_kv_heads.  The reference keeps K as [H, D, T]
+ * (kernels.py:144-145); here K and V share the token-major [H, T, D] layout,
+ * which makes every key row one 2*head_dim-byte line for TMA and bulk copies.
+ *
+ * Plan metadata is one int32 device buffer holding the arrays described by
+ * ta_plan_layout (offsets in int32 elements from `meta`).  The first six are
+ * the reference's own arrays from prepare() (kernels.py:103-141), bit-exact:
+ *   qids   [num_jobs, max_requests]   request ids of each job, zero padded
+ *   kstart [num_jobs, kstart_stride]  first physical position of each job
+ *   qlen   [num_jobs]                 requests per job
+ *   klen   [num_jobs]                 positions per job (mutable, see below)
+ *   slots  [num_requests, max_slots]  reference slot code job*max_requests+j
+ *   counts [num_requests]             partials per request
+ * followed by this implementation's own arrays:
+ *   slot_base   [num_jobs]                 first compact partial of each job
+ *   cslots      [num_requests, max_slots]  compact partial ids per request
+ *   small_tasks [num_small_tasks, 2]       (job, 16-row tile) for the SIMT kernel
+ *   tc_tasks    [num_tc_tasks, 2]          (job, 128-row tile) for the tcgen05 kernel
+ *
+ * Return value: 0 on success, otherwise a TA_ERR_* code describing a rejected
+ * argument or a launch failure.  Errors found on the device (a metadata index
+ * out of range, a bounded wait that gave up) are OR-ed into *status (a device
+ * int32 the caller owns and zeroes; may be NULL) and never trap.
+ */
+#ifndef TREE_ATTN_H
+#define TREE_ATTN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TA_ABI_VERSION 1
+
+#define TA_DTYPE_BF16 1
+#define TA_DTYPE_F16 2
+
+#define TA_OK 0
+#define TA_ERR_ARG 1          /* host: invalid argument, nothing launched */
+#define TA_ERR_LAUNCH 2       /* host: a kernel launch failed */
+#define TA_ERR_BOUNDS 4       /* device: plan index out of range, access skipped */
+#define TA_ERR_TIMEOUT 8      /* device: a bounded wait gave up */
+#define TA_ERR_UNSUPPORTED 16 /* host: shape or dtype without a kernel */
+
+typedef struct ta_plan_layout {
+  int32_t num_jobs;
+  int32_t max_requests;
+  int32_t max_slots;
+  int32_t num_requests;
+  int32_t num_partials;
+  int32_t num_small_tasks;
+  int32_t num_tc_tasks;
+  /* small tasks are sorted by padded row count: [0, e0) need 4 rows,
+     [e0, e1) 8 rows, [e1, e2) 16 rows; e2 == num_small_tasks */
+  int32_t small_class_end[3];
+  int32_t kstart_stride;
+  int32_t off_qids;
+  int32_t off_kstart;
+  int32_t off_qlen;
+  int32_t off_klen;
+  int32_t off_slots;
+  int32_t off_counts;
+  int32_t off_slot_base;
+  int32_t off_cslots;
+  int32_t off_small_tasks;
+  int32_t off_tc_tasks;
+} ta_plan_layout;
+
+/* ABI version of the loaded library (TA_ABI_VERSION). */
+int ta_abi_version(void);
+
+/* Human-readable name of a TA_ERR_* code or status bit set. */
+const char* ta_error_string(int code);
+
+/*
+ * Partial attention of every (job, KV head) of the plan: for each query row
+ * (request of the job x GQA row) the softmax-normalised output over the job's
+ * positions and its natural-log LSE, written to part/lse at the row's compact
+ * partial slot.  A job with zero positions writes O = 0 and LSE = -inf.
+ * Replaces the reference's _segment kernel (kernels.py:8-55) and its two launch
+ * phases in attention_matrix (kernels.py:158-165).
+ */
+int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, const void* kpool,
+               const void* vpool, int64_t pool_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+               int32_t head_dim, int32_t dtype, float* part, float* lse, int32_t* status, void* stream);
+
+/*
+ * Global log-sum-exp merge of each request's partials into out (dtype of q);
+ * out_lse [num_requests, num_q_heads] f32 receives the merged LSE when not
+ * NULL.  Partials with LSE = -inf contribute nothing; a request whose partials
+ * are all empty gets O = 0.  Replaces the reference's _merge kernel
+ * (kernels.py:58-83) launched at kernels.py:166-167.
+ */
+int ta_merge(const ta_plan_layout* plan, const int32_t* meta, const float* part, const float* lse,
+             void* out, float* out_lse, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+             int32_t dtype, int32_t* status, void* stream);
+
+/*
+ * ta_segment followed by ta_merge on the same stream: the whole decode-step
+ * attention of attention_matrix (kernels.py:152-168).
+ */
+int ta_attention(const ta_plan_layout* plan, const int32_t* meta, const void* q, const void* kpool,
+                 const void* vpool, int64_t pool_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                 int32_t head_dim, int32_t dtype, float* part, float* lse, void* out, float* out_lse,
+                 int32_t* status, void* stream);
+
+/*
+ * klen[tail_jobs[i]] = value for i < num_tails, on the device: the per-step
+ * update of a reused decode plan, CachedDecodePlan.update (kernels.py:184-186).
+ */
+int ta_update_tail_klen(int32_t* klen, const int32_t* tail_jobs, int32_t num_tails, int32_t value,
+                        int32_t num_jobs, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TREE_ATTN_H */

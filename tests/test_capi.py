@@ -1,0 +1,62 @@
+"""The C-ABI library: loads without a GPU and exports every symbol the header declares."""
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from tree_attention import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "tree_attn.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(ta_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declarations_match_binding():
+    assert declared_functions() == sorted(_lib.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r" T (ta_\w+)$", out, flags=re.M))
+    assert set(declared_functions()) <= exported
+
+
+def test_abi_version_and_error_strings():
+    lib = _lib.load()
+    assert lib.ta_abi_version() == _lib.ABI_VERSION
+    assert lib.ta_error_string(0) == b"ok"
+    assert lib.ta_error_string(_lib.ERR_BOUNDS).startswith(b"plan index")
+
+
+def test_argument_validation_without_gpu():
+    """Rejected arguments return an error code before any CUDA call."""
+    lib = _lib.load()
+    layout = _lib.PlanLayout()
+    layout.kstart_stride = 1
+    assert lib.ta_segment(None, None, None, None, None, 0, 32, 8, 128, 1, None, None, None, None) == _lib.ERR_ARG
+    # 6 query heads over 4 KV heads is not a GQA grouping
+    assert lib.ta_segment(layout, 1024, None, None, None, 0, 6, 4, 128, 1, None, None, None,
+                          None) == _lib.ERR_UNSUPPORTED
+    assert lib.ta_merge(layout, 1024, None, None, None, None, 32, 8, 48, 1, None, None) == _lib.ERR_UNSUPPORTED
+    assert lib.ta_update_tail_klen(None, None, -1, 0, 0, None, None) == _lib.ERR_ARG
+    # an empty plan is a no-op
+    assert lib.ta_segment(layout, 1024, None, None, None, 0, 32, 8, 128, 1, None, None, None, None) == 0
+
+
+def test_layout_struct_matches_header():
+    import ctypes
+    text = HEADER.read_text()
+    body = text[text.index("typedef struct ta_plan_layout"):text.index("} ta_plan_layout;")]
+    names = re.findall(r"int32_t (\w+)(?:\[(\d+)\])?;", body)
+    fields = [(n, int(c) if c else 1) for n, c in names]
+    assert [(f[0], getattr(f[1], "_length_", 1)) for f in _lib.PlanLayout._fields_] == fields
+    assert ctypes.sizeof(_lib.PlanLayout) == 4 * sum(c for _, c in fields)

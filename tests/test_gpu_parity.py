@@ -1,0 +1,242 @@
+"""Kernel parity on a B200: the CUDA path through the C ABI against the FP32 oracle.
+
+Tolerances (north-star criteria): per-(request, head) relative L2 <= 5e-3 of
+the BF16 output against the FP32 oracle, |dLSE| <= 1e-3 in natural-log units;
+plus the reference's own benchmark check atol .008 / rtol .03
+(scripts/benchmark.py:96 of the reference).
+"""
+import os
+
+import pytest
+import torch
+
+from oracle import attention as oracle
+from tree_attention import CostModel, KVTree, schedule
+from tree_attention import kernels
+from tree_attention.kernels import CachedDecodePlan, attention_matrix, check_status, pack_kv, prepare
+from tests.golden.make_golden import TREE_SPECS, build_tree
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 5e-3
+LSE_TOL = 1e-3
+SPECS = {s["name"]: s for s in TREE_SPECS}
+
+
+class _Lib:
+    KVTree = KVTree
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    os.environ["TREE_ATTN_CHECK"] = "1"
+    yield
+    os.environ.pop("TREE_ATTN_CHECK", None)
+
+
+def make_inputs(nreq, storage, hq, hk, d, dtype, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(nreq, hq, d, generator=g) * scale).to(dtype)
+    k = torch.randn(storage, hk, d, generator=g).to(dtype)
+    v = torch.randn(storage, hk, d, generator=g).to(dtype)
+    return q, k, v
+
+
+def rel_l2(actual, expected):
+    err = (actual.float() - expected.float()).flatten(2).norm(dim=-1)
+    ref = expected.float().flatten(2).norm(dim=-1).clamp_min(1e-30)
+    return (err / ref)
+
+
+def run_kernel(q, k, v, plan, pool_pad=0, pad_value=float("nan")):
+    dev = "cuda"
+    qd = q.to(dev)
+    kp, vp = pack_kv(k.to(dev), v.to(dev))
+    if pool_pad:
+        # capacity beyond the used positions holds garbage (NaN) that must never be read
+        pad = torch.full((kp.shape[0], pool_pad, kp.shape[2]), pad_value, dtype=kp.dtype, device=dev)
+        kp = torch.cat([kp, pad], 1).contiguous()
+        vp = torch.cat([vp, pad], 1).contiguous()
+    p = prepare(plan, qd)
+    lse = torch.empty(q.shape[0], q.shape[1], device=dev, dtype=torch.float32)
+    out = attention_matrix(qd, kp, vp, p, out_lse=lse)
+    torch.cuda.synchronize()
+    check_status(p)
+    return out.cpu(), lse.cpu(), p
+
+
+def check_against_oracle(q, k, v, paths, out, lse):
+    _, ref_f, ref_lse = oracle.request_attention(q.float(), k.float(), v.float(), paths, return_lse=True)
+    err = rel_l2(out, ref_f)
+    assert torch.isfinite(out.float()).all()
+    assert err.max().item() <= REL_L2, f"max rel L2 {err.max().item():.3e}"
+    assert (lse - ref_lse).abs().max().item() <= LSE_TOL
+    torch.testing.assert_close(out.float(), ref_f.to(out.dtype).float(), atol=.008, rtol=.03)
+
+
+TREES = ["unequal_nested_terminal", "no_shared_prefix", "deep_synthetic", "duplicate_terminal", "wide",
+         "extension", "small_config1", "deep_bench", "no_share_root0", "decode_tree"]
+
+
+@pytest.mark.parametrize("name", TREES)
+@pytest.mark.parametrize("heads", [(32, 8, 128), (8, 2, 64), (8, 2, 32)], ids=["h32x8d128", "h8x2d64", "h8x2d32"])
+def test_tree_plans_match_oracle(name, heads):
+    hq, hk, d = heads
+    tree = build_tree(_Lib, SPECS[name])
+    q, k, v = make_inputs(len(tree.paths), tree.storage_tokens, hq, hk, d, torch.bfloat16, seed=101)
+    for model in (CostModel(), CostModel(kv_split=48), CostModel.b200()):
+        for method in ("request", "fixed", "greedy", "cube"):
+            plan = schedule(tree, hq, hk, d, method, model)
+            out, lse, _ = run_kernel(q, k, v, plan, pool_pad=37)
+            check_against_oracle(q, k, v, tree.paths, out, lse)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_reference_check_trees(dtype):
+    """The reference's scripts/check_npu.py:12-31 trees, both dtypes, kv_split=128."""
+    trees = {
+        "unequal": KVTree.synthetic([-1, 0, 0, 1, 1], [129, 65, 17, 33, 81], [2, 3, 4]),
+        "none": KVTree.from_sequences([[1, 2, 3], [4], [5, 6, 7, 8, 9]]),
+        "duplicate_terminal": KVTree.from_sequences([[1, 2], [1, 2], [1, 2, 3, 4], [1, 5, 6]]),
+        "wide": KVTree.synthetic([-1] + [0] * 32, [257] + [31 + i for i in range(32)], list(range(1, 33))),
+    }
+    for tree in trees.values():
+        q, k, v = make_inputs(len(tree.paths), tree.storage_tokens, 8, 2, 64, dtype, seed=2026)
+        for method in ("request", "fixed", "greedy", "cube"):
+            plan = schedule(tree, 8, 2, 64, method, CostModel(kv_split=128))
+            out, lse, _ = run_kernel(q, k, v, plan)
+            check_against_oracle(q, k, v, tree.paths, out, lse)
+
+
+def test_extreme_logits():
+    """Scores scaled x30 stress the LSE merge (reference tests/test_semantics.py:19-21)."""
+    tree = build_tree(_Lib, SPECS["deep_synthetic"])
+    q, k, v = make_inputs(len(tree.paths), tree.storage_tokens, 8, 2, 32, torch.bfloat16, seed=17, scale=30.0)
+    for method in ("request", "fixed", "greedy", "cube"):
+        plan = schedule(tree, 8, 2, 32, method, CostModel(kv_split=48))
+        out, lse, _ = run_kernel(q, k, v, plan)
+        check_against_oracle(q, k, v, tree.paths, out, lse)
+
+
+def test_segment_partials_match_oracle():
+    """Each (job, request) partial output and LSE, read back from the scratch buffers."""
+    tree = build_tree(_Lib, SPECS["deep_bench"])
+    q, k, v = make_inputs(len(tree.paths), tree.storage_tokens, 32, 8, 128, torch.bfloat16, seed=5)
+    plan = schedule(tree, 32, 8, 128, "cube", CostModel(kv_split=200))
+    _, _, p = run_kernel(q, k, v, plan)
+    part, lse = p.part.cpu(), p.lse.cpu()
+    expected = oracle.job_partials(q.float(), k.float(), v.float(), p.jobs)
+    base = p.host_arrays["slot_base"]
+    for i, (job, (o_ref, l_ref)) in enumerate(zip(p.jobs, expected)):
+        for j in range(len(job.requests)):
+            rows = slice((base[i] + j) * 4, (base[i] + j + 1) * 4)
+            o = part[:, rows].reshape(32, 128)      # [HK*G, D] == query heads in order
+            l = lse[:, rows].reshape(32)
+            assert ((o - o_ref[j]).norm(dim=-1) / o_ref[j].norm(dim=-1)).max() <= REL_L2
+            assert (l - l_ref[j]).abs().max() <= LSE_TOL
+
+
+def test_large_group_rows():
+    """256 requests sharing one prefix: a job of 1024 query rows (many row tiles)."""
+    tree = KVTree.synthetic([-1] + [0] * 256, [700] + [3 + (i % 5) for i in range(256)], list(range(1, 257)))
+    q, k, v = make_inputs(256, tree.storage_tokens, 32, 8, 128, torch.bfloat16, seed=9)
+    plan = schedule(tree, 32, 8, 128, "cube", CostModel.b200())
+    out, lse, _ = run_kernel(q, k, v, plan, pool_pad=300)
+    check_against_oracle(q, k, v, tree.paths, out, lse)
+
+
+def test_cached_decode_plan_matches_oracle():
+    """Prompt plan reused over decode steps with growing private tails (incl. length 0)."""
+    base = KVTree.synthetic([-1, 0, 0, 0, 0] + [1 + i // 2 for i in range(8)], [300, 100, 90, 80, 70] + [40] * 8,
+                            list(range(5, 13)))
+    steps = 5
+    prefix = base.storage_tokens
+    q, k, v = make_inputs(8, prefix + 8 * steps, 32, 8, 128, torch.bfloat16, seed=301)
+    qd = q.cuda()
+    kp, vp = pack_kv(k.cuda(), v.cuda())
+    cached = CachedDecodePlan(schedule(base, method="cube", model=CostModel(kv_split=128)), qd, prefix, steps)
+    assert cached.tail_indices.numel() == 8
+    for n in (0, 1, 3, steps):
+        p = cached.update(n)
+        lse = torch.empty(8, 32, device="cuda")
+        out = attention_matrix(qd, kp, vp, p, out_lse=lse).cpu()
+        torch.cuda.synchronize()
+        check_status(p)
+        paths = [path + tuple(prefix + r * steps + t for t in range(n)) for r, path in enumerate(base.paths)]
+        check_against_oracle(q, k, v, paths, out, lse.cpu())
+
+
+def test_graph_capture_replays_same_result():
+    tree = build_tree(_Lib, SPECS["small_config1"])
+    q, k, v = make_inputs(8, tree.storage_tokens, 32, 8, 128, torch.bfloat16, seed=3)
+    qd = q.cuda()
+    kp, vp = pack_kv(k.cuda(), v.cuda())
+    p = prepare(schedule(tree, method="cube", model=CostModel.b200()), qd)
+    eager = attention_matrix(qd, kp, vp, p).clone()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    os.environ["TREE_ATTN_CHECK"] = "0"
+    try:
+        with torch.cuda.graph(graph, stream=stream):
+            attention_matrix(qd, kp, vp, p)
+    finally:
+        os.environ["TREE_ATTN_CHECK"] = "1"
+    p.out.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    check_status(p)
+    assert torch.equal(p.out, eager)
+
+
+def test_bounds_violation_is_reported_not_trapped():
+    """A pool shorter than the plan's positions: the kernel skips the read and flags it.
+
+    The real allocation is larger than the claimed pool length, so even an
+    unchecked access would stay inside memory this process owns.
+    """
+    tree = KVTree.synthetic([-1, 0, 0], [64, 16, 16], [1, 2])
+    q, k, v = make_inputs(2, tree.storage_tokens, 32, 8, 128, torch.bfloat16, seed=4)
+    qd = q.cuda()
+    kp, vp = pack_kv(k.cuda(), v.cuda())
+    p = prepare(schedule(tree, method="fixed"), qd)
+    lib = kernels._lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.ta_attention(p.layout, p.metadata.data_ptr(), qd.data_ptr(), kp.data_ptr(), vp.data_ptr(), 70,
+                          32, 8, 128, kernels._lib.DTYPE_BF16, p.part.data_ptr(), p.lse.data_ptr(),
+                          p.out.data_ptr(), None, p.status.data_ptr(), stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(p.status.item()) & kernels._lib.ERR_BOUNDS
+    assert torch.isfinite(p.out.float()).all()
+    p.status.zero_()
+
+
+def test_headline_full_size_properties():
+    """Full BASELINE headline shape: tree plans agree with the per-request plan, and a
+    sample of requests agrees with the FP32 oracle."""
+    tree = KVTree.synthetic([-1] + [0] * 128, [8128] + [64] * 128, list(range(1, 129)))
+    q, k, v = make_inputs(128, tree.storage_tokens, 32, 8, 128, torch.bfloat16, seed=101)
+    qd = q.cuda()
+    kp, vp = pack_kv(k.cuda(), v.cuda())
+    outs = {}
+    for method, model in (("request", CostModel()), ("fixed", CostModel()), ("cube", CostModel()),
+                          ("cube", CostModel.b200()), ("greedy", CostModel.b200())):
+        p = prepare(schedule(tree, method=method, model=model), qd)
+        lse = torch.empty(128, 32, device="cuda")
+        outs[(method, model.kv_split)] = (attention_matrix(qd, kp, vp, p, out_lse=lse).clone(), lse)
+        torch.cuda.synchronize()
+        check_status(p)
+    base_out, base_lse = outs[("request", 512)]
+    for key, (o, l) in outs.items():
+        assert rel_l2(o.cpu(), base_out.cpu()).max() <= REL_L2, key
+        assert (l - base_lse).abs().max().item() <= LSE_TOL, key
+    sample = [0, 1, 63, 127]
+    sub_paths = [tree.paths[r] for r in sample]
+    _, ref_f, ref_lse = oracle.request_attention(q[sample].float(), k.float(), v.float(), sub_paths,
+                                                 return_lse=True)
+    o, l = outs[("cube", CostModel.b200().kv_split)]
+    assert rel_l2(o.cpu()[sample], ref_f).max() <= REL_L2
+    assert (l.cpu()[sample] - ref_lse).abs().max() <= LSE_TOL

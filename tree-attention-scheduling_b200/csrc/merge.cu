@@ -1,0 +1,147 @@
+// Global log-sum-exp merge of each request's partials (reference _merge,
+// kernels.py:58-83), plus the tiny device update of a reused decode plan.
+//
+// One warp per (request, query head).  Instead of the reference's serial
+// running-max loop, lane k first loads the LSE of partial k so the maximum and
+// the weights come from two warp reductions; the partial rows are then read
+// with independent 16-byte loads (lanes split head_dim).
+#include "ta_common.cuh"
+#include "ta_kernels.cuh"
+
+namespace ta {
+
+namespace {
+
+constexpr int kMergeWarps = 4;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) {
+  constexpr int DL = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
+  if (item >= p.num_requests * p.num_q_heads) return;
+  const int request = item / p.num_q_heads, head = item % p.num_q_heads;
+  const int G = p.group, kv_head = head / G, g = head % G;
+
+  int count = p.counts[request];
+  if (count < 0 || count > p.max_slots) {
+    if (lane == 0) set_status(p.status, TA_ERR_BOUNDS);
+    count = 0;
+  }
+  const int32_t* slots = p.cslots + int64_t(request) * p.max_slots;
+  const int64_t head_rows = int64_t(kv_head) * p.num_partials;
+
+  auto row_of = [&](int k, bool& ok) -> int64_t {
+    const int s = slots[k];
+    ok = s >= 0 && s < p.num_partials;
+    return (head_rows + (ok ? s : 0)) * G + g;
+  };
+
+  // pass 1: maximum LSE over the request's partials
+  float m = -INFINITY;
+  for (int k0 = 0; k0 < count; k0 += 32) {
+    float l = -INFINITY;
+    if (k0 + lane < count) {
+      bool ok;
+      const int64_t row = row_of(k0 + lane, ok);
+      if (ok) l = p.lse[row];
+      else set_status(p.status, TA_ERR_BOUNDS);
+    }
+    m = fmaxf(m, warp_max(l));
+  }
+
+  // pass 2: weights exp(lse - m) and the weighted sum of partial rows
+  float acc[DL];
+#pragma unroll
+  for (int e = 0; e < DL; ++e) acc[e] = 0.f;
+  float z = 0.f;
+  if (m != -INFINITY) {
+    for (int k0 = 0; k0 < count; k0 += 32) {
+      float w = 0.f;
+      bool ok = false;
+      if (k0 + lane < count) {
+        const int64_t row = row_of(k0 + lane, ok);
+        if (ok) w = fast_exp2((p.lse[row] - m) * kLog2e);  // -inf lse gives 0
+      }
+      z += warp_sum(w);
+      const int n = min(32, count - k0);
+      for (int j = 0; j < n; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, w, j);
+        if (wj == 0.f) continue;  // empty partial: its row may hold anything
+        bool okj;
+        const int64_t row = row_of(k0 + j, okj);
+        const float* src = p.part + row * D + lane * DL;
+        if constexpr (DL == 4) {
+          const float4 x = *reinterpret_cast<const float4*>(src);
+          acc[0] = fmaf(wj, x.x, acc[0]); acc[1] = fmaf(wj, x.y, acc[1]);
+          acc[2] = fmaf(wj, x.z, acc[2]); acc[3] = fmaf(wj, x.w, acc[3]);
+        } else if constexpr (DL == 2) {
+          const float2 x = *reinterpret_cast<const float2*>(src);
+          acc[0] = fmaf(wj, x.x, acc[0]); acc[1] = fmaf(wj, x.y, acc[1]);
+        } else {
+          acc[0] = fmaf(wj, src[0], acc[0]);
+        }
+      }
+    }
+  }
+  const float inv = z > 0.f ? 1.f / z : 0.f;
+  uint16_t* out = reinterpret_cast<uint16_t*>(p.out) + (int64_t(request) * p.num_q_heads + head) * D + lane * DL;
+  if constexpr (DL == 4) {
+    uint2 bits;
+    bits.x = Elem<T>::pack2(acc[0] * inv, acc[1] * inv);
+    bits.y = Elem<T>::pack2(acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<uint2*>(out) = bits;
+  } else if constexpr (DL == 2) {
+    *reinterpret_cast<uint32_t*>(out) = Elem<T>::pack2(acc[0] * inv, acc[1] * inv);
+  } else {
+    *out = Elem<T>::from_float(acc[0] * inv);
+  }
+  if (p.out_lse && lane == 0) {
+    p.out_lse[int64_t(request) * p.num_q_heads + head] = z > 0.f ? m + fast_log2(z) * kLn2 : -INFINITY;
+  }
+}
+
+__global__ void fill_klen_kernel(int32_t* klen, const int32_t* idx, int n, int value, int num_jobs,
+                                 int32_t* status) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int j = idx[i];
+  if (j < 0 || j >= num_jobs) {
+    set_status(status, TA_ERR_BOUNDS);
+    return;
+  }
+  klen[j] = value;
+}
+
+template <typename T, int D>
+cudaError_t launch_merge_typed(const MergeParams& p, cudaStream_t stream) {
+  const int items = p.num_requests * p.num_q_heads;
+  if (items == 0) return cudaSuccess;
+  const int blocks = (items + kMergeWarps - 1) / kMergeWarps;
+  merge_kernel<T, D><<<blocks, kMergeWarps * 32, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_merge(const MergeParams& p, int head_dim, int dtype, cudaStream_t stream) {
+  if (dtype == TA_DTYPE_BF16) {
+    if (head_dim == 128) return launch_merge_typed<__nv_bfloat16, 128>(p, stream);
+    if (head_dim == 64) return launch_merge_typed<__nv_bfloat16, 64>(p, stream);
+    if (head_dim == 32) return launch_merge_typed<__nv_bfloat16, 32>(p, stream);
+  } else if (dtype == TA_DTYPE_F16) {
+    if (head_dim == 128) return launch_merge_typed<__half, 128>(p, stream);
+    if (head_dim == 64) return launch_merge_typed<__half, 64>(p, stream);
+    if (head_dim == 32) return launch_merge_typed<__half, 32>(p, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_fill_klen(int32_t* klen, const int32_t* idx, int n, int value, int num_jobs, int32_t* status,
+                             cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  fill_klen_kernel<<<(n + 127) / 128, 128, 0, stream>>>(klen, idx, n, value, num_jobs, status);
+  return cudaGetLastError();
+}
+
+}  // namespace ta

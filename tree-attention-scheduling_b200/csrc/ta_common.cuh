@@ -1,0 +1,171 @@
+// Shared device helpers for the tree-attention kernels (sm_100a only).
+//
+// Every wait on an mbarrier is bounded: after TA_SPIN_LIMIT polls the waiting
+// thread records TA_ERR_TIMEOUT in the call's status word and gives up, so a
+// lost completion can never hang the GPU.  Index checks on plan metadata record
+// TA_ERR_BOUNDS and skip the access instead of trapping.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "tree_attn.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "tree-attention kernels target sm_100a only"
+#endif
+
+namespace ta {
+
+// Polls of mbarrier.try_wait before a wait is declared lost.  Each poll may
+// suspend the thread for a hardware-chosen interval; 2^26 polls is on the order
+// of seconds, far above any legitimate wait in these kernels.
+constexpr uint32_t TA_SPIN_LIMIT = 1u << 26;
+
+__device__ __forceinline__ void set_status(int32_t* status, int32_t bit) {
+  if (status) atomicOr(status, bit);
+}
+
+// ---------------------------------------------------------------------------
+// element types
+template <typename T> struct Elem;
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int kCode = TA_DTYPE_BF16;
+  __device__ __forceinline__ static float2 to_float2(uint32_t bits) {
+    // bf16 -> f32 is exact: the bf16 bits are the high half of the f32.
+    return make_float2(__uint_as_float(bits << 16), __uint_as_float(bits & 0xffff0000u));
+  }
+  __device__ __forceinline__ static float to_float(uint16_t bits) {
+    return __uint_as_float(uint32_t(bits) << 16);
+  }
+  __device__ __forceinline__ static uint16_t from_float(float x) {
+    __nv_bfloat16 h = __float2bfloat16_rn(x);
+    return *reinterpret_cast<uint16_t*>(&h);
+  }
+  __device__ __forceinline__ static uint32_t pack2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct Elem<__half> {
+  static constexpr int kCode = TA_DTYPE_F16;
+  __device__ __forceinline__ static float2 to_float2(uint32_t bits) {
+    __half2 h = *reinterpret_cast<__half2*>(&bits);
+    return __half22float2(h);
+  }
+  __device__ __forceinline__ static float to_float(uint16_t bits) {
+    __half h = *reinterpret_cast<__half*>(&bits);
+    return __half2float(h);
+  }
+  __device__ __forceinline__ static uint16_t from_float(float x) {
+    __half h = __float2half_rn(x);
+    return *reinterpret_cast<uint16_t*>(&h);
+  }
+  __device__ __forceinline__ static uint32_t pack2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// exp2 on the SFU: softmax runs in the log2 domain (scores are pre-scaled by
+// log2(e)/sqrt(D)), the LSE is converted back to natural-log units on output.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_log2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ---------------------------------------------------------------------------
+// shared-memory addresses and mbarriers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`.  Returns false (and records the
+// timeout) if the phase never completed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
+  for (uint32_t i = 0; i < TA_SPIN_LIMIT; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  set_status(status, TA_ERR_TIMEOUT);
+  return false;
+}
+
+// 1-D bulk copy global -> shared, completing on `bar` (non-multicast).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Warp transpose-reduction: lane l ends up with the sum over all lanes of
+// v[l].  31 shuffles for 32 sums (versus 5 per sum for a plain butterfly).
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? v[i] : v[i + off];
+      const float keep = upper ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
+  return x;
+}
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  return x;
+}
+
+}  // namespace ta

@@ -1,0 +1,102 @@
+"""ctypes binding of the C ABI in ``include/tree_attn.h``.
+
+The shared library is built in-tree by ``build.py`` (``libtree_attn_b200.so``
+next to this file).  There is no fallback: if the library is missing or was
+built for another ABI version, every kernel entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libtree_attn_b200.so")
+ABI_VERSION = 1
+
+DTYPE_BF16 = 1
+DTYPE_F16 = 2
+
+ERR_ARG = 1
+ERR_LAUNCH = 2
+ERR_BOUNDS = 4
+ERR_TIMEOUT = 8
+ERR_UNSUPPORTED = 16
+
+STATUS_NAMES = {ERR_ARG: "invalid argument", ERR_LAUNCH: "kernel launch failed",
+                ERR_BOUNDS: "plan index out of range on the device",
+                ERR_TIMEOUT: "bounded device wait gave up",
+                ERR_UNSUPPORTED: "shape or dtype not supported"}
+
+# Every symbol declared in include/tree_attn.h.
+EXPORTS = ("ta_abi_version", "ta_error_string", "ta_segment", "ta_merge", "ta_attention",
+           "ta_update_tail_klen")
+
+
+class PlanLayout(ctypes.Structure):
+    """Mirror of ``ta_plan_layout``."""
+    _fields_ = [
+        ("num_jobs", ctypes.c_int32),
+        ("max_requests", ctypes.c_int32),
+        ("max_slots", ctypes.c_int32),
+        ("num_requests", ctypes.c_int32),
+        ("num_partials", ctypes.c_int32),
+        ("num_small_tasks", ctypes.c_int32),
+        ("num_tc_tasks", ctypes.c_int32),
+        ("small_class_end", ctypes.c_int32 * 3),
+        ("kstart_stride", ctypes.c_int32),
+        ("off_qids", ctypes.c_int32),
+        ("off_kstart", ctypes.c_int32),
+        ("off_qlen", ctypes.c_int32),
+        ("off_klen", ctypes.c_int32),
+        ("off_slots", ctypes.c_int32),
+        ("off_counts", ctypes.c_int32),
+        ("off_slot_base", ctypes.c_int32),
+        ("off_cslots", ctypes.c_int32),
+        ("off_small_tasks", ctypes.c_int32),
+        ("off_tc_tasks", ctypes.c_int32),
+    ]
+
+
+def describe_status(code):
+    if code == 0:
+        return "ok"
+    return ", ".join(name for bit, name in STATUS_NAMES.items() if code & bit) or f"status {code}"
+
+
+_lib = None
+
+
+def load():
+    """Load the kernel library once; raise if it is absent or mismatched."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = os.environ.get("TREE_ATTN_LIB", str(LIB_PATH))
+    if not Path(path).exists():
+        raise RuntimeError(f"tree-attention kernel library not found at {path}; "
+                           "build it with `python tree-attention-scheduling_b200/build.py`")
+    lib = ctypes.CDLL(path)
+    P, I32, I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    LP = ctypes.POINTER(PlanLayout)
+    lib.ta_abi_version.restype = ctypes.c_int
+    lib.ta_abi_version.argtypes = []
+    lib.ta_error_string.restype = ctypes.c_char_p
+    lib.ta_error_string.argtypes = [ctypes.c_int]
+    lib.ta_segment.restype = ctypes.c_int
+    lib.ta_segment.argtypes = [LP, P, P, P, P, I64, I32, I32, I32, I32, P, P, P, P]
+    lib.ta_merge.restype = ctypes.c_int
+    lib.ta_merge.argtypes = [LP, P, P, P, P, P, I32, I32, I32, I32, P, P]
+    lib.ta_attention.restype = ctypes.c_int
+    lib.ta_attention.argtypes = [LP, P, P, P, P, I64, I32, I32, I32, I32, P, P, P, P, P, P]
+    lib.ta_update_tail_klen.restype = ctypes.c_int
+    lib.ta_update_tail_klen.argtypes = [P, P, I32, I32, I32, P, P]
+    version = lib.ta_abi_version()
+    if version != ABI_VERSION:
+        raise RuntimeError(f"kernel library ABI {version}, expected {ABI_VERSION}; rebuild it")
+    _lib = lib
+    return lib
+
+
+def check(rc, what):
+    if rc != 0:
+        raise RuntimeError(f"{what} failed: {describe_status(rc)} (code {rc})")
