@@ -314,7 +314,7 @@ def run_b200(args):
 
     sampler = ClockSampler(local)
     sampler.start()
-    burn_end = time.perf_counter() + args.burn_s
+    burn_end = time.perf_counter() + (0.0 if args.quick else args.burn_s)
     while time.perf_counter() < burn_end:       # sustained load so the clock samples see the step
         flush.zero_()
         step.segment()
@@ -328,7 +328,7 @@ def run_b200(args):
 
     # other plans on the same kernels (same shards), for the speed-up columns
     for method, m in (("request", CostModel()), ("fixed", model), ("greedy", model)):
-        if not args.all_plans and method != "request":
+        if args.quick or (not args.all_plans and method != "request"):
             continue
         pl = kernels.prepare(schedule(tree, HQ, HK, D, method, m), q, num_kv_heads=len(heads))
         s, mg = time_step(Step(q, kp, vp, pl), max(3, args.steps // 2), args.warmup, flush, world)
@@ -336,7 +336,7 @@ def run_b200(args):
         del pl
 
     q_host = q.cpu().pin_memory()
-    e2e_us, h2d, d2h = time_e2e(q_host, step, args.steps, args.warmup, flush, world)
+    e2e_us, h2d, d2h = time_e2e(q_host, step, 1 if args.quick else args.steps, args.warmup, flush, world)
     e2e_us = max_over_ranks(e2e_us, world)
     kernels.check_status(prepared)
 
@@ -375,7 +375,7 @@ def run_b200(args):
     }
     if "request" in results:
         line["per_request_speedup"] = round(results["request"]["step_us"] / step_us, 3)
-    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+    if world == 1 and rank == 0 and not (args.no_cpu_baseline or args.quick):
         cpu_us, n, threads = cpu_oracle_step_us(tree, plan, q, kp, vp, budget_s=args.cpu_budget_s)
         line["cpu_baseline"] = {"value": round(total_bytes / (cpu_us * 1e-6) / 1e9, 4), "unit": "GB/s",
                                 "step_us": round(cpu_us, 1), "cores": threads, "kind": "port",
@@ -433,6 +433,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--burn-s", type=float, default=1.0, help="sustained untimed load before timing (clocks)")
+    ap.add_argument("--quick", action="store_true",
+                    help="main plan only: no burn, other plans, CPU baseline or repeated e2e (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

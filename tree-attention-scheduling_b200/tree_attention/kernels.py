@@ -52,7 +52,7 @@ def tc_supported(head_dim, dtype):
 
 
 # Set once the tcgen05 kernel is part of the library.
-_TC_BUILT = False
+_TC_BUILT = True
 
 
 @dataclass
