@@ -240,3 +240,18 @@ def test_headline_full_size_properties():
     o, l = outs[("cube", CostModel.b200().kv_split)]
     assert rel_l2(o.cpu()[sample], ref_f).max() <= REL_L2
     assert (l.cpu()[sample] - ref_lse).abs().max() <= LSE_TOL
+
+
+@pytest.mark.parametrize("keys", [1, 100, 128, 129, 256, 384, 512, 640, 1000, 2048, 2600])
+@pytest.mark.parametrize("nreq", [5, 32, 40])
+def test_tensor_core_pipeline_tile_counts(keys, nreq):
+    """One shared segment read by nreq requests (tensor-core path for > 16 rows)
+    with 1..21 key tiles: every ring wrap-around and barrier phase of the
+    pipeline, full and partial last tiles, NaN in the pool past the segment."""
+    tree = KVTree.synthetic([-1], [keys], [0] * nreq)
+    q, k, v = make_inputs(nreq, keys, 32, 8, 128, torch.bfloat16, seed=keys * 7 + nreq)
+    plan = schedule(tree, 32, 8, 128, "fixed", CostModel(kv_split=4096, max_query_rows=4096))
+    out, lse, p = run_kernel(q, k, v, plan, pool_pad=200)
+    if nreq * 4 > kernels.SMALL_ROWS:
+        assert p.layout.num_tc_tasks == (nreq * 4 + kernels.TC_ROWS - 1) // kernels.TC_ROWS
+    check_against_oracle(q, k, v, tree.paths, out, lse)

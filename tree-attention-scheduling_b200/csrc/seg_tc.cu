@@ -1,22 +1,42 @@
 // Segment attention for large groups on the 5th-generation tensor cores.
 //
-// Work of one CTA: one (job, 128-row query tile, KV head).  The query tile
-// stacks the GQA rows of up to 32 requests that share the job's KV segment, so
-// S = Q K^T and O = P V are dense 128 x 128 x 128 contractions per 128-key tile:
+// Work of one CTA: one (job, 256-row query pair, KV head).  The query rows
+// stack the GQA rows of the requests that share the job's KV segment; they are
+// split into two 128-row tiles A and B that consume every K/V tile together,
+// so each 64 KB K/V tile fetched through L2 feeds four 128 x 128 x 128 MMAs
+// (the L2-to-SM path, about 8 TB/s, is what bounds a kernel that streams the
+// tiles once per 128 rows).
 //
-//   warp 0      TMA producer: K and V tiles (token-major pools, 2 x 64-column
-//               boxes with 128-byte swizzle, no multicast), 2-stage ring
-//   warp 1      TMEM owner + MMA issuer: tcgen05.mma kind::f16, A and B from
-//               shared memory, S double-buffered in TMEM, O accumulated in TMEM
-//   warps 2-5   softmax: one query row per thread (TMEM lane), S read with
-//               tcgen05.ld, exp2 on pre-scaled scores, P written to shared
-//               memory as bf16/f16 in the canonical K-major 128B-swizzle layout;
-//               O is rescaled in TMEM only when a row's running max grows by
-//               more than 2^8 (otherwise the stale max is kept, which is exact
-//               after the final division); epilogue O / z and the LSE.
+//   warp 0      TMA producer of K tiles (token-major pool, 2 x 64-column boxes
+//               with 128-byte swizzle, no multicast), 2-stage ring (an optional
+//               L2 prefetch kPrefetch tiles ahead is off by default)
+//   warp 10     TMA producer of V tiles, likewise; it also zeroes the rows of
+//               the segment's last V tile that lie past the segment
+//   warp 1      one thread issues every tcgen05.mma: S_t = Q_t K^T (A = Q_t and
+//               B = K from shared memory) and O_t += P_t V (A = P_t from TMEM,
+//               written by softmax over its own S_t; B = V from shared memory),
+//               in the order S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) ...
+//               so the tensor pipe works on one tile while softmax works on the
+//               other
+//   warps 2-9   softmax: two threads per query row (TMEM lane), each owning 64
+//               key columns, alternating between tiles A and B; row maxima are
+//               exchanged through shared memory with a named barrier per lane
+//               quadrant; exp2 on pre-scaled scores, a third of them by a
+//               polynomial on the FMA pipe; P packed to bf16/f16 pairs and
+//               stored to TMEM.  O_t is rescaled in TMEM only when a row's
+//               running max grows by more than 2^8 (otherwise the stale max is
+//               kept, which is exact after the final division).  Epilogue:
+//               O_t / z and the natural-log LSE per row.
 //
-// TMEM columns: [0,128) S0, [128,256) S1, [256,384) O.  Shared memory: Q 32 KB,
-// K 2 x 32 KB, V 2 x 32 KB, P 32 KB.  All waits are bounded (ta_common.cuh).
+// Ordering facts the barrier scheme relies on: tcgen05.mma operations issued
+// by one thread execute in issue order, so S_t(j+1) cannot overwrite P_t(j)
+// before P_t(j) V(j) has read it, and observing S_t(j) complete implies
+// P_t(j-1) V(j-1) has completed (it was issued just before S_t(j)).  No waiter
+// can fall two phases behind a barrier, so parity waits never alias.
+//
+// TMEM columns: [0,128) S_A / P_A, [128,256) S_B / P_B, [256,384) O_A,
+// [384,512) O_B.  Shared memory: Q_A, Q_B 2 x 32 KB, K 2 x 32 KB, V 2 x 32 KB.
+// All waits are bounded (ta_common.cuh).
 //
 // The reference's _segment (kernels.py:8-55) computes the same partial O / LSE
 // with Triton tiles of 64 query rows x 64 keys.
@@ -30,31 +50,40 @@ namespace ta {
 
 namespace {
 
-constexpr int kRows = 128;      // query rows per CTA (MMA M)
-constexpr int kKeys = 128;      // keys per tile (MMA N of S, K of P.V)
+constexpr int kRows = 128;      // query rows per tile (MMA M); a CTA holds two tiles
+constexpr int kKeys = 128;      // keys per K/V tile (MMA N of S, K of P.V)
 constexpr int kDim = 128;       // head_dim (MMA K of S, N of P.V)
-constexpr int kStages = 2;
-constexpr int kThreads = 192;
-constexpr uint32_t kTileBytes = kKeys * kDim * 2;       // 32 KB per K or V tile
+constexpr int kKStages = 2;
+constexpr int kVStages = 2;
+constexpr int kPrefetch = 0;   // L2 prefetch distance in tiles (0: off; a 6-tile burst delayed the first loads)
+constexpr int kSoftmaxWarps = 8;
+constexpr int kVProducerWarp = 2 + kSoftmaxWarps;
+constexpr int kThreads = (3 + kSoftmaxWarps) * 32;
+constexpr int kHalfCols = kKeys / 2;                     // key columns per softmax thread
+constexpr uint32_t kTileBytes = kKeys * kDim * 2;       // 32 KB per K, V or Q tile
 constexpr uint32_t kHalfBytes = kTileBytes / 2;         // one 64-column swizzled block
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColO = 256;
+constexpr uint32_t kColS = 0, kColO = 256;              // + tile * 128
 constexpr float kRescaleThreshold = 8.0f;               // log2 units
 
 struct TcSmem {
-  static constexpr uint32_t off_q = 0;
-  static constexpr uint32_t off_k = off_q + kTileBytes;
-  static constexpr uint32_t off_v = off_k + kStages * kTileBytes;
-  static constexpr uint32_t off_p = off_v + kStages * kTileBytes;
-  static constexpr uint32_t off_bar = off_p + kTileBytes;
-  // barriers: k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], q_full, p_full, pv_done
-  static constexpr int kBars = 13;
+  static constexpr uint32_t off_q = 0;                                 // Q_A, Q_B
+  static constexpr uint32_t off_k = off_q + 2 * kTileBytes;
+  static constexpr uint32_t off_v = off_k + kKStages * kTileBytes;
+  // [tile][3 slots][2 half][128 rows] f32: slots 0/1 row maxima by tile
+  // parity, slot 2 denominators
+  static constexpr uint32_t off_xchg = off_v + kVStages * kTileBytes;
+  static constexpr uint32_t off_bar = off_xchg + 2 * 3 * 2 * kRows * 4;
+  static constexpr int kBars = 18;
   static constexpr uint32_t off_tmem = off_bar + kBars * 8;
   static constexpr uint32_t bytes = off_tmem + 16;
   static constexpr uint32_t alloc = bytes + 1024;         // slack to align the base to 1 KB
 };
 
-enum Bar { K_FULL = 0, V_FULL = 2, KV_EMPTY = 4, S_FULL = 6, S_FREE = 8, Q_FULL = 10, P_FULL = 11, PV_DONE = 12 };
+// k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[A,B], p_full[A,B], pv_done[A,B], q_full, v_tail
+enum Bar {
+  K_FULL = 0, K_EMPTY = 2, V_FULL = 4, V_EMPTY = 6, S_FULL = 8, P_FULL = 10, PV_DONE = 12, Q_FULL = 14, V_TAIL = 15
+};
 
 // ---- UMMA descriptors -------------------------------------------------------
 // Shared-memory matrix descriptor (sm_100): start>>4 [0,14), LBO>>4 [16,30),
@@ -69,20 +98,29 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   return d;
 }
 
-// Instruction descriptor, kind::f16: D f32, A/B f16 (0) or bf16 (1), both
-// operands from shared memory, M = 128, N = 128; b_mn_major selects an
-// N-contiguous B (the V tile).
+// Instruction descriptor, kind::f16: D f32, A/B f16 (0) or bf16 (1), K-major
+// A, M = 128, N = 128; b_mn_major selects an N-contiguous B (the V tile).
 __host__ __device__ constexpr uint32_t instr_desc(uint32_t ab_format, uint32_t b_mn_major) {
   return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (b_mn_major << 16) | ((uint32_t(kKeys) >> 3) << 17) |
          ((uint32_t(kRows) >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D (TMEM) (+)= A (smem) * B (smem)
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
       ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// D (TMEM) (+)= A (TMEM) * B (smem)
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -94,37 +132,38 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 32 consecutive f32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// Named barrier among `count` threads (id 0 is __syncthreads).
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+#define TA_REGS32(r) "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), \
+  "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),                \
+  "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),              \
+  "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+#define TA_VALS32(r) "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), \
+  "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),                \
+  "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),              \
+  "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
       "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : TA_REGS32(r)
       : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
       "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
-      ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31])));
+      ::"r"(taddr), TA_VALS32(r));
 }
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Bounded wait whose outcome is the same for every lane of the warp, so the
 // warp-collective tcgen05 instructions that follow never run diverged.
@@ -133,8 +172,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_
   return __all_sync(0xffffffffu, ok);
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
   asm volatile(
@@ -142,6 +185,65 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       "[%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+
+// Maximum of 64 values as a balanced tree (short dependency chains).
+__device__ __forceinline__ float max64(const float (&s)[kHalfCols]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(fmaxf(s[i], s[i + 8]), fmaxf(s[i + 16], s[i + 24]));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], fmaxf(fmaxf(s[i + 32], s[i + 40]), fmaxf(s[i + 48], s[i + 56])));
+  return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+}
+
+// Packed pairs of f32 (sm_100 FFMA2 / FADD2): half the issue slots.
+union F2 {
+  unsigned long long u;
+  float2 f;
+};
+__device__ __forceinline__ F2 ffma2(F2 a, F2 b, F2 c) {
+  F2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.u) : "l"(a.u), "l"(b.u), "l"(c.u));
+  return d;
+}
+__device__ __forceinline__ F2 fadd2(F2 a, F2 b) {
+  F2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d.u) : "l"(a.u), "l"(b.u));
+  return d;
+}
+__device__ __forceinline__ F2 fsub2(F2 a, F2 b) {
+  F2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d.u) : "l"(a.u), "l"(b.u));
+  return d;
+}
+__device__ __forceinline__ F2 splat(float x) {
+  F2 r;
+  r.f = make_float2(x, x);
+  return r;
+}
+
+// 2^x for a pair on the FMA pipe: x = n + f with n = round(x) via the
+// 1.5 * 2^23 shift and f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose
+// coefficients are a Remez (minimax relative error) fit computed for this
+// kernel, max relative error 7.5e-5 -- far below the 2^-9 rounding of the
+// bf16 P it feeds; 2^n is added to the exponent field.  Arguments are clamped
+// at -125, so a masked key (-inf) yields 2^-125 instead of 0: such keys only
+// occur past the end of a segment, where the V rows are zeroed, and 2^-125 is
+// far below the resolution of the row sum.
+__device__ __forceinline__ F2 poly_exp2x2(F2 x) {
+  F2 xc;
+  xc.f = make_float2(fmaxf(x.f.x, -125.f), fmaxf(x.f.y, -125.f));
+  const F2 t = fadd2(xc, splat(12582912.f));                 // 1.5 * 2^23
+  const F2 f = fsub2(xc, fsub2(t, splat(12582912.f)));
+  F2 p = ffma2(splat(0.0551716685295105f), f, splat(0.2426111251115799f));
+  p = ffma2(p, f, splat(0.6932609677314758f));
+  p = ffma2(p, f, splat(0.9999280571937561f));
+  const int nx = __float_as_int(t.f.x) - 0x4B400000, ny = __float_as_int(t.f.y) - 0x4B400000;
+  F2 r;
+  r.f = make_float2(__int_as_float(__float_as_int(p.f.x) + (nx << 23)),
+                    __int_as_float(__float_as_int(p.f.y) + (ny << 23)));
+  return r;
 }
 
 // Byte offset of 16-byte chunk `c` (0..15 over a 128-element row) of row `r`
@@ -157,13 +259,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::off_bar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::off_tmem);
+  float* xchg = reinterpret_cast<float*>(smem + TcSmem::off_xchg);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int task = blockIdx.x, head = blockIdx.y;
   const int G = p.group;
 
   const int job = p.tc_tasks[2 * task];
-  const int tile = p.tc_tasks[2 * task + 1];
+  const int pair = p.tc_tasks[2 * task + 1];
   if (job < 0 || job >= p.num_jobs) {
     if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
     return;
@@ -171,8 +274,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nr = p.qlen[job];
   int nk = p.klen[job];
   const int64_t k0 = p.kstart[int64_t(job) * p.kstart_stride];
-  const int r0 = tile * kRows;
-  const int rows = min(kRows, nr * G - r0);
+  const int r0 = pair * 2 * kRows;
+  const int rows = min(2 * kRows, nr * G - r0);            // rows of this pair
+  const int ntile = rows > kRows ? 2 : 1;                  // tile B present?
   const int64_t part_row0 = int64_t(p.slot_base[job]) * G + r0;
   const bool rows_ok = rows > 0 && part_row0 >= 0 && part_row0 + rows <= int64_t(p.num_partials) * G;
   if (!rows_ok || nr > p.max_requests || nk < 0 || k0 < 0 || k0 + nk > p.pool_tokens || k0 > INT32_MAX - kKeys) {
@@ -190,18 +294,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars[K_FULL + s], 1);
-      mbar_init(&bars[V_FULL + s], 1);
-      mbar_init(&bars[KV_EMPTY + s], 1);
-    }
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[K_FULL + s], 1);
+      mbar_init(&bars[K_EMPTY + s], 1);
+      mbar_init(&bars[V_FULL + s], 1);
+      mbar_init(&bars[V_EMPTY + s], 1);
       mbar_init(&bars[S_FULL + s], 1);
-      mbar_init(&bars[S_FREE + s], 4);
+      mbar_init(&bars[P_FULL + s], kSoftmaxWarps);
+      mbar_init(&bars[PV_DONE + s], 1);
     }
-    mbar_init(&bars[Q_FULL], 4);
-    mbar_init(&bars[P_FULL], 4);
-    mbar_init(&bars[PV_DONE], 1);
+    mbar_init(&bars[Q_FULL], kSoftmaxWarps);
+    mbar_init(&bars[V_TAIL], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -215,106 +318,146 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   bool alive = true;
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
+  if (warp == 0 || warp == kVProducerWarp) {
+    // ---------------- TMA producers (K ring / V ring) ----------------
+    const bool is_k = warp == 0;
     if (lane == 0) {
-      for (int j = 0; j < ntiles && alive; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages && !mbar_wait(&bars[KV_EMPTY + st], ((j / kStages) + 1) & 1, p.status)) {
-          alive = false;
-          break;
+      const int stages = is_k ? kKStages : kVStages;
+      const CUtensorMap* map = is_k ? &tmap_k : &tmap_v;
+      unsigned char* ring = smem + (is_k ? TcSmem::off_k : TcSmem::off_v);
+      uint64_t* full = &bars[is_k ? K_FULL : V_FULL];
+      uint64_t* empty = &bars[is_k ? K_EMPTY : V_EMPTY];
+      for (int j = 0; j < min(ntiles, kPrefetch); ++j) {
+        tma_prefetch_l2(map, 0, int(k0) + j * kKeys, head);
+        tma_prefetch_l2(map, 64, int(k0) + j * kKeys, head);
+      }
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % stages;
+        if (j + kPrefetch < ntiles) {
+          tma_prefetch_l2(map, 0, int(k0) + (j + kPrefetch) * kKeys, head);
+          tma_prefetch_l2(map, 64, int(k0) + (j + kPrefetch) * kKeys, head);
         }
+        if (j >= stages && !mbar_wait(&empty[st], ((j / stages) + 1) & 1, p.status)) break;
         const int y = int(k0) + j * kKeys;
-        unsigned char* kdst = smem + TcSmem::off_k + st * kTileBytes;
-        unsigned char* vdst = smem + TcSmem::off_v + st * kTileBytes;
-        mbar_arrive_expect_tx(&bars[K_FULL + st], kTileBytes);
-        tma_load_3d(kdst, &tmap_k, 0, y, head, &bars[K_FULL + st]);
-        tma_load_3d(kdst + kHalfBytes, &tmap_k, 64, y, head, &bars[K_FULL + st]);
-        mbar_arrive_expect_tx(&bars[V_FULL + st], kTileBytes);
-        tma_load_3d(vdst, &tmap_v, 0, y, head, &bars[V_FULL + st]);
-        tma_load_3d(vdst + kHalfBytes, &tmap_v, 64, y, head, &bars[V_FULL + st]);
+        unsigned char* dst = ring + st * kTileBytes;
+        mbar_arrive_expect_tx(&full[st], kTileBytes);
+        tma_load_3d(dst, map, 0, y, head, &full[st]);
+        tma_load_3d(dst + kHalfBytes, map, 64, y, head, &full[st]);
+      }
+    }
+    if (!is_k) {
+      // Keys past the segment in its last tile: their P is 0 but their V rows
+      // may hold anything (NaN in unwritten pool capacity), so zero them once
+      // the tile has landed and publish it on V_TAIL instead of V_FULL.
+      const int last = ntiles - 1, last_keys = nk - last * kKeys;
+      if (last_keys < kKeys) {
+        const int st = last % kVStages;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars[V_FULL + st], (last / kVStages) & 1, p.status));
+        if (ok) {
+          unsigned char* vtile = smem + TcSmem::off_v + st * kTileBytes;
+          for (int i = lane; i < (kKeys - last_keys) * 16; i += 32) {
+            const int r = last_keys + i / 16, c = i % 16;
+            *reinterpret_cast<uint4*>(vtile + (c >> 3) * kHalfBytes + r * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[V_TAIL]);
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    constexpr uint32_t ab = Elem<T>::kCode == TA_DTYPE_BF16 ? 1u : 0u;
-    constexpr uint32_t idesc_s = instr_desc(ab, 0);
-    constexpr uint32_t idesc_o = instr_desc(ab, 1);
-    const uint32_t q_addr = smem_u32(smem + TcSmem::off_q);
-    const uint32_t p_addr = smem_u32(smem + TcSmem::off_p);
-    const int last_keys = nk - (ntiles - 1) * kKeys;
+    // One thread and as few instructions as possible: this warp shares its SM
+    // sub-partition with two busy softmax warps.  Descriptors are precomputed;
+    // per MMA only the 14-bit start-address field of the low word changes
+    // (shared addresses < 256 KB never carry out of it).
+    if (lane == 0) {
+      constexpr uint32_t ab = Elem<T>::kCode == TA_DTYPE_BF16 ? 1u : 0u;
+      constexpr uint32_t idesc_s = instr_desc(ab, 0);
+      constexpr uint32_t idesc_o = instr_desc(ab, 1);
+      const uint64_t qdesc0 = smem_desc(smem_u32(smem + TcSmem::off_q), 16, 1024);
+      const uint64_t kdesc0 = smem_desc(smem_u32(smem + TcSmem::off_k), 16, 1024);
+      const uint64_t vdesc0 = smem_desc(smem_u32(smem + TcSmem::off_v), kHalfBytes, 1024);
+      const bool tail = nk - (ntiles - 1) * kKeys < kKeys;
 
-    auto issue_pv = [&](int j) -> bool {
-      const int st = j % kStages;
-      if (!warp_wait(&bars[P_FULL], j & 1, p.status)) return false;
-      if (!warp_wait(&bars[V_FULL + st], (j / kStages) & 1, p.status)) return false;
-      unsigned char* vtile = smem + TcSmem::off_v + st * kTileBytes;
-      if (j == ntiles - 1 && last_keys < kKeys) {
-        // keys past the segment: their P is 0 but their V rows may hold
-        // anything (NaN in unwritten pool capacity), so zero them.
-        for (int i = lane; i < (kKeys - last_keys) * 16; i += 32) {
-          const int r = last_keys + i / 16, c = i % 16;
-          *reinterpret_cast<uint4*>(vtile + (c >> 3) * kHalfBytes + r * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
-        }
-        fence_async_smem();
-        __syncwarp();
-      }
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t v_addr = smem_u32(vtile);
-#pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k) {
-          // A = P: 16 keys = 32 bytes along the swizzled row; B = V (N-major):
-          // 16 keys = two 8-row atoms = 2048 bytes; LBO = 64-column block stride.
-          const uint64_t a = smem_desc(p_addr + (k >> 2) * kHalfBytes + (k & 3) * 32, 16, 1024);
-          const uint64_t b = smem_desc(v_addr + k * 2048, kHalfBytes, 1024);
-          umma(tmem + kColO, a, b, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(&bars[PV_DONE]);
-        umma_commit(&bars[KV_EMPTY + st]);
-      }
-      __syncwarp();
-      return true;
-    };
-
-    if (!warp_wait(&bars[Q_FULL], 0, p.status)) alive = false;
-    for (int j = 0; j < ntiles && alive; ++j) {
-      const int st = j % kStages, sb = j & 1;
-      if (!warp_wait(&bars[K_FULL + st], (j / kStages) & 1, p.status)) { alive = false; break; }
-      if (j >= 2 && !warp_wait(&bars[S_FREE + sb], ((j >> 1) + 1) & 1, p.status)) { alive = false; break; }
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t k_addr = smem_u32(smem + TcSmem::off_k + st * kTileBytes);
+      auto issue_s = [&](int t, int j) {   // S_t(j) = Q_t K(j)^T
+        const uint64_t qd = qdesc0 + uint64_t(t) * (kTileBytes >> 4);
+        const uint64_t kd = kdesc0 + uint64_t(j % kKStages) * (kTileBytes >> 4);
 #pragma unroll
         for (int k = 0; k < kDim / 16; ++k) {
-          const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
-          umma(tmem + kColS0 + sb * kKeys, smem_desc(q_addr + off, 16, 1024), smem_desc(k_addr + off, 16, 1024),
-               idesc_s, k > 0 ? 1u : 0u);
+          // 16 dims = 32 bytes along the swizzled K-major rows of Q and K
+          const uint64_t off = ((k >> 2) * kHalfBytes + (k & 3) * 32) >> 4;
+          umma_ss(tmem + kColS + t * kKeys, qd + off, kd + off, idesc_s, k > 0 ? 1u : 0u);
         }
-        umma_commit(&bars[S_FULL + sb]);
+        umma_commit(&bars[S_FULL + t]);
+      };
+      auto issue_pv = [&](int t, int j) {  // O_t += P_t(j) V(j)
+        const uint64_t vd = vdesc0 + uint64_t(j % kVStages) * (kTileBytes >> 4);
+        const uint32_t p_tmem = tmem + kColS + t * kKeys;
+#pragma unroll
+        for (int k = 0; k < kKeys / 16; ++k)
+          // A = P in TMEM (16 keys = 8 packed columns); B = V, N-major: 16 keys
+          // = two 8-row atoms = 2048 bytes; LBO = 64-column block stride.
+          umma_ts(tmem + kColO + t * kDim, p_tmem + k * 8, vd + ((k * 2048) >> 4), idesc_o,
+                  (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&bars[PV_DONE + t]);
+      };
+
+      if (!mbar_wait(&bars[Q_FULL], 0, p.status)) alive = false;
+      if (alive && !mbar_wait(&bars[K_FULL], 0, p.status)) alive = false;
+      if (alive) {
+        tc_fence_after();
+        issue_s(0, 0);
+        if (ntile == 2) issue_s(1, 0);
+        umma_commit(&bars[K_EMPTY]);
       }
-      __syncwarp();
-      if (j >= 1 && !issue_pv(j - 1)) { alive = false; break; }
+      for (int j = 0; j < ntiles && alive; ++j) {
+        const bool more = j + 1 < ntiles;
+        const bool zeroed = tail && j == ntiles - 1;
+        for (int t = 0; t < ntile; ++t) {
+          if (!mbar_wait(&bars[P_FULL + t], j & 1, p.status)) { alive = false; break; }
+          if (t == 0 && !mbar_wait(&bars[zeroed ? V_TAIL : V_FULL + j % kVStages],
+                                   zeroed ? 0 : (j / kVStages) & 1, p.status)) { alive = false; break; }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (t == ntile - 1) umma_commit(&bars[V_EMPTY + j % kVStages]);
+          if (more) {
+            if (t == 0) {
+              if (!mbar_wait(&bars[K_FULL + (j + 1) % kKStages], ((j + 1) / kKStages) & 1, p.status)) {
+                alive = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            issue_s(t, j + 1);
+            if (t == ntile - 1) umma_commit(&bars[K_EMPTY + (j + 1) % kKStages]);
+          }
+        }
+      }
+      // The last commits' arrivals must land before the CTA's shared memory
+      // is released: wait for the final release of each ring slot.
+      if (alive) {
+        for (int j = max(0, ntiles - kKStages); j < ntiles; ++j)
+          if (!mbar_wait(&bars[K_EMPTY + j % kKStages], (j / kKStages) & 1, p.status)) break;
+        for (int j = max(0, ntiles - kVStages); j < ntiles; ++j)
+          if (!mbar_wait(&bars[V_EMPTY + j % kVStages], (j / kVStages) & 1, p.status)) break;
+      }
     }
-    if (alive && !issue_pv(ntiles - 1)) alive = false;
-    // The last commits' arrivals must land before the CTA's shared memory is
-    // released: wait for the final release of each stage.
-    if (alive) {
-      for (int j = max(0, ntiles - kStages); j < ntiles; ++j)
-        if (!warp_wait(&bars[KV_EMPTY + j % kStages], (j / kStages) & 1, p.status)) break;
-    }
-  } else {
+  } else if (warp >= 2 && warp < 2 + kSoftmaxWarps) {
     // ---------------- softmax / correction / epilogue ----------------
-    const int quad = warp & 3;                 // TMEM lane quadrant of this warp
-    const int row = quad * 32 + lane;          // query row of this thread
+    const int quad = warp & 3;                       // TMEM lane quadrant of this warp
+    const int half = (warp - 2) >> 2;                // which 64 key columns of the row
+    const int row = quad * 32 + lane;                // query row of this thread within a tile
     const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);
 
-    // Q row -> shared memory (K-major, 128B swizzle), zero for padding rows.
-    {
-      unsigned char* qs = smem + TcSmem::off_q;
+    // Q half-rows of both tiles -> shared memory (K-major, 128B swizzle),
+    // zero for padding rows.
+    for (int t = 0; t < 2; ++t) {
+      unsigned char* qs = smem + TcSmem::off_q + t * kTileBytes;
+      const int trow = t * kRows + row;              // row within the pair
       const uint4* src = nullptr;
-      if (row < rows) {
-        const int grow = r0 + row;
+      if (trow < rows) {
+        const int grow = r0 + trow;
         const int rid = p.qids[int64_t(job) * p.max_requests + grow / G];
         if (rid >= 0 && rid < p.num_requests)
           src = reinterpret_cast<const uint4*>(p.q + (int64_t(rid) * p.num_q_heads + head * G + grow % G) * kDim);
@@ -322,108 +465,130 @@ __global__ void __launch_bounds__(kThreads, 1)
           set_status(p.status, TA_ERR_BOUNDS);
       }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint4 v = src ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(qs + swz_offset(row, c)) = v;
+      for (int c = 0; c < 8; ++c) {
+        const int chunk = half * 8 + c;
+        const uint4 v = src ? src[chunk] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(qs + swz_offset(row, chunk)) = v;
       }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[Q_FULL]);
     }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars[Q_FULL]);
 
     const float scale = p.scale_log2;
-    float m_run = -INFINITY, z = 0.f;
-    unsigned char* ps = smem + TcSmem::off_p;
+    float m_run[2] = {-INFINITY, -INFINITY}, z[2] = {0.f, 0.f};
     for (int j = 0; j < ntiles && alive; ++j) {
-      const int sb = j & 1;
-      if (!warp_wait(&bars[S_FULL + sb], (j >> 1) & 1, p.status)) { alive = false; break; }
-      tc_fence_after();
-      float s[kKeys];
-#pragma unroll
-      for (int c = 0; c < kKeys / 32; ++c) {
-        float chunk[32];
-        tmem_ld32(lane_addr + kColS0 + sb * kKeys + c * 32, chunk);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = chunk[i];
-      }
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[S_FREE + sb]);
-
-      const int valid = min(kKeys, nk - j * kKeys);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < kKeys; ++i) {
-        if (i >= valid) s[i] = -INFINITY;
-        mx = fmaxf(mx, s[i]);
-      }
-      const float m_tile = mx * scale;          // valid >= 1, so finite
-      float m_new = m_run;
-      bool rescale = false;
-      if (j == 0) {
-        m_new = m_tile;
-      } else if (m_tile > m_run + kRescaleThreshold) {
-        m_new = m_tile;
-        rescale = true;
-      }
-      // P buffer and O are free once the previous P.V has completed.
-      if (j >= 1 && !warp_wait(&bars[PV_DONE], (j - 1) & 1, p.status)) { alive = false; break; }
-      tc_fence_after();
-      if (__any_sync(0xffffffffu, rescale)) {
-        const float alpha = rescale ? fast_exp2(m_run - m_new) : 1.f;
-        z *= alpha;
-#pragma unroll
-        for (int c = 0; c < kDim / 32; ++c) {
-          float o[32];
-          tmem_ld32(lane_addr + kColO + c * 32, o);
+      const int valid = min(kKeys, nk - j * kKeys) - half * kHalfCols;   // may be <= 0 for the upper half
+      for (int t = 0; t < ntile; ++t) {
+        const uint32_t s_col = kColS + t * kKeys;
+        float* my_x = xchg + t * (3 * 2 * kRows);    // [slot][half][row] of this tile
+        if (!warp_wait(&bars[S_FULL + t], j & 1, p.status)) { alive = false; break; }
+        tc_fence_after();
+        float s[kHalfCols];
+        {
+          uint32_t a[32], b[32];
+          tmem_ld32(lane_addr + s_col + half * kHalfCols, a);
+          tmem_ld32(lane_addr + s_col + half * kHalfCols + 32, b);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(lane_addr + kColO + c * 32, o);
+          for (int i = 0; i < 32; ++i) {
+            s[i] = __uint_as_float(a[i]);
+            s[i + 32] = __uint_as_float(b[i]);
+          }
         }
+        if (valid < kHalfCols) {
+#pragma unroll
+          for (int i = 0; i < kHalfCols; ++i)
+            if (i >= valid) s[i] = -INFINITY;
+        }
+        // row max across the two halves (both threads have finished reading S,
+        // so P may overwrite it after this barrier)
+        const int slot = j & 1;
+        my_x[(slot * 2 + half) * kRows + row] = max64(s);
+        named_sync(1 + quad, 64);
+        const float mx = fmaxf(my_x[(slot * 2 + 0) * kRows + row], my_x[(slot * 2 + 1) * kRows + row]);
+        const float m_tile = mx * scale;             // at least one key is valid: finite
+        float m_new = m_run[t];
+        bool rescale = false;
+        if (j == 0) {
+          m_new = m_tile;
+        } else if (m_tile > m_run[t] + kRescaleThreshold) {
+          m_new = m_tile;
+          rescale = true;
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O_t holds P_t(j-1) V(j-1) already: S_t(j) was issued after it.
+          const float alpha = rescale ? fast_exp2(m_run[t] - m_new) : 1.f;
+          z[t] *= alpha;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t o[32];
+            tmem_ld32(lane_addr + kColO + t * kDim + half * kHalfCols + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(lane_addr + kColO + t * kDim + half * kHalfCols + c * 32, o);
+          }
+        }
+        m_run[t] = m_new;
+        uint32_t packed[32];
+        F2 sum = splat(0.f);
+        const F2 sc = splat(scale), neg_m = splat(-m_new);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          F2 x;
+          x.f = make_float2(s[2 * i], s[2 * i + 1]);
+          x = ffma2(x, sc, neg_m);
+          F2 e;
+          if (i % 3 == 2) {               // every third pair on the FMA pipe, the rest on the SFU
+            e = poly_exp2x2(x);
+          } else {
+            e.f = make_float2(fast_exp2(x.f.x), fast_exp2(x.f.y));
+          }
+          sum = fadd2(sum, e);
+          packed[i] = Elem<T>::pack2(e.f.x, e.f.y);
+        }
+        z[t] += sum.f.x + sum.f.y;
+        // P over this thread's half of S_t: key columns [64h, 64h+64) ->
+        // packed columns [32h, 32h+32).
+        tmem_st32(lane_addr + s_col + half * 32, packed);
         tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[P_FULL + t]);
       }
-      m_run = m_new;
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < kKeys / 8; ++c) {
-        uint32_t packed[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float a = fast_exp2(fmaf(s[c * 8 + 2 * i], scale, -m_run));
-          const float b = fast_exp2(fmaf(s[c * 8 + 2 * i + 1], scale, -m_run));
-          sum += a + b;
-          packed[i] = Elem<T>::pack2(a, b);
-        }
-        *reinterpret_cast<uint4*>(ps + swz_offset(row, c)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      }
-      z += sum;
-      fence_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[P_FULL]);
     }
 
-    // epilogue: wait for the last P.V, then O / z and the natural-log LSE
-    if (alive && !warp_wait(&bars[PV_DONE], (ntiles - 1) & 1, p.status)) alive = false;
-    tc_fence_after();
-    const float inv = (alive && z > 0.f) ? 1.f / z : 0.f;
-    float* dst = p.part + (head_rows + part_row0 + row) * kDim;
+    // epilogue per tile: wait for its last P.V, then O / z and the LSE.
+    // Observing S_t(ntiles-1) implied P_t(ntiles-2) V done, so PV_DONE_t is at
+    // most one phase behind this wait.
+    for (int t = 0; t < ntile; ++t) {
+      if (alive && !warp_wait(&bars[PV_DONE + t], (ntiles - 1) & 1, p.status)) alive = false;
+      tc_fence_after();
+      float* my_x = xchg + t * (3 * 2 * kRows);
+      my_x[(4 + half) * kRows + row] = z[t];
+      named_sync(1 + quad, 64);
+      const float z_all = my_x[(4 + 0) * kRows + row] + my_x[(4 + 1) * kRows + row];
+      const float inv = (alive && z_all > 0.f) ? 1.f / z_all : 0.f;
+      const int trow = t * kRows + row;
+      float* dst = p.part + (head_rows + part_row0 + trow) * kDim + half * kHalfCols;
 #pragma unroll
-    for (int c = 0; c < kDim / 32; ++c) {
-      float o[32];
-      tmem_ld32(lane_addr + kColO + c * 32, o);
-      tmem_wait_ld();
-      if (row < rows) {
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        tmem_ld32(lane_addr + kColO + t * kDim + half * kHalfCols + c * 32, o);
+        tmem_wait_ld();
+        if (trow < rows) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(dst + c * 32 + i) =
-              make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dst + c * 32 + i) =
+                make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                            __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+        }
       }
+      if (trow < rows && half == 0)
+        p.lse[head_rows + part_row0 + trow] =
+            (alive && z_all > 0.f) ? (m_run[t] + fast_log2(z_all)) * kLn2 : -INFINITY;
     }
-    if (row < rows)
-      p.lse[head_rows + part_row0 + row] = (alive && z > 0.f) ? (m_run + fast_log2(z)) * kLn2 : -INFINITY;
   }
 
   tc_fence_before();

@@ -10,6 +10,6 @@ B200_CONSTANTS = dict(
     merge_us=0.002,
     cube_rows=16,
     key_tile=256,
-    kv_split=2048,
+    kv_split=1024,
     max_query_rows=512,
 )

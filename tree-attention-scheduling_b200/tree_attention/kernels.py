@@ -38,7 +38,7 @@ from .schedule import Job, Plan, physical_jobs
 # Query rows a small-group (SIMT) task covers; larger jobs go to the tensor-core
 # kernel in tiles of TC_ROWS rows when it supports the shape.
 SMALL_ROWS = 16
-TC_ROWS = 128
+TC_ROWS = 256
 # Reference sort key: jobs with more than 16 query rows run in the second phase
 # (kernels.py:109-110).  Kept verbatim so the metadata is bit-identical.
 _REF_SMALL_ROWS = 16
