@@ -9,9 +9,11 @@ one decode query per request; subset-DP ("cube") plan with the B200 cost model.
 One step = one decode-step attention: the segment kernels over every
 (job, KV head) plus the LSE merge, inputs resident in HBM.  Metric: physical-KV
 HBM throughput (physical KV bytes / step time, GB/s, higher is better); the
-step latency in microseconds is reported beside it.  The KV working set
-(66.8 MB) fits in the 126 MB L2, so a 512 MB buffer is overwritten between
-timed steps (L2 flush) outside the timed events.
+step latency in microseconds is reported beside it.  The KV working set of one
+step (66.8 MB) fits in the 126 MB L2, so consecutive steps rotate through
+COPIES independent copies of the queries and pools (4 x 67 MB, larger than L2):
+every step reads its KV from HBM, with no flush kernel in the timed region.
+The K timed steps are one CUDA graph replay, timed with CUDA events.
 
 With ``--gpus N`` (launched by torchrun, one process per GPU) the 8 KV heads are
 sharded: rank r owns heads [r*8/N, (r+1)*8/N) with their query heads and that
@@ -48,7 +50,7 @@ METRIC = "tree-attn decode step µs & physical-KV HBM GB/s, 128req×8K ctx, 1–
 NREQ, ROOT_LEN, LEAF_LEN = 128, 8128, 64
 HQ, HK, D = 32, 8, 128
 SEED = 101
-FLUSH_BYTES = 512 << 20
+COPIES = 4
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
@@ -185,24 +187,25 @@ def barrier(world):
 
 
 class Step:
-    """One decode step of a prepared plan, split into segment and merge launches."""
+    """One decode step of a prepared plan over one of several input copies."""
 
-    def __init__(self, q, kp, vp, prepared):
-        self.q, self.kp, self.vp, self.p = q, kp, vp, prepared
+    def __init__(self, copies, prepared):
+        self.copies, self.p = copies, prepared
+        self.q, self.kp, self.vp = copies[0]
         self.lib = _lib.load()
         L = prepared.layout
         self.launches = (sum(1 for i, e in enumerate(L.small_class_end) if e > (L.small_class_end[i - 1] if i else 0))
                          + (1 if L.num_tc_tasks else 0) + 1)
 
-    def segment(self):
+    def segment(self, copy=0):
         p = self.p
-        rc = self.lib.ta_segment(p.layout, p.metadata.data_ptr(), self.q.data_ptr(), self.kp.data_ptr(),
-                                 self.vp.data_ptr(), self.kp.shape[1], self.q.shape[1], self.kp.shape[0], D,
-                                 _lib.DTYPE_BF16, p.part.data_ptr(), p.lse.data_ptr(), p.status.data_ptr(),
-                                 torch.cuda.current_stream().cuda_stream)
+        q, kp, vp = self.copies[copy]
+        rc = self.lib.ta_segment(p.layout, p.metadata.data_ptr(), q.data_ptr(), kp.data_ptr(), vp.data_ptr(),
+                                 kp.shape[1], q.shape[1], kp.shape[0], D, _lib.DTYPE_BF16, p.part.data_ptr(),
+                                 p.lse.data_ptr(), p.status.data_ptr(), torch.cuda.current_stream().cuda_stream)
         _lib.check(rc, "ta_segment")
 
-    def merge(self):
+    def merge(self, copy=0):
         p = self.p
         rc = self.lib.ta_merge(p.layout, p.metadata.data_ptr(), p.part.data_ptr(), p.lse.data_ptr(),
                                p.out.data_ptr(), None, self.q.shape[1], self.kp.shape[0], D, _lib.DTYPE_BF16,
@@ -223,51 +226,52 @@ def capture(fn):
     return graph
 
 
-def time_step(step, steps, warmup, flush, world, use_graph=True):
-    """Device time (µs) per step of the segment phase and the merge, L2 flushed between steps."""
-    if use_graph:
-        g_seg, g_merge = capture(step.segment), capture(step.merge)
-        seg, merge = g_seg.replay, g_merge.replay
-    else:
-        seg, merge = step.segment, step.merge
+def time_graph(graph, units, warmup, world):
+    """Device microseconds per unit of one replay of `graph` (after `warmup` replays)."""
     for _ in range(warmup):
-        flush.zero_()
-        seg()
-        merge()
+        graph.replay()
     barrier(world)
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
-    for e0, e1, e2 in events:
-        flush.zero_()
-        e0.record()
-        seg()
-        e1.record()
-        merge()
-        e2.record()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    graph.replay()
+    e1.record()
     barrier(world)
-    seg_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in events)
-    merge_ms = sum(e1.elapsed_time(e2) for _, e1, e2 in events)
-    return seg_ms * 1e3 / steps, merge_ms * 1e3 / steps
+    return e0.elapsed_time(e1) * 1e3 / units
 
 
-def time_e2e(q_host, step, steps, warmup, flush, world):
+def time_step(step, steps, warmup, world):
+    """Device time (us) per step: K whole steps in one graph, then the segment
+    launches and the merge alone (for the per-kernel roofline), all rotating
+    through the input copies so every step streams its KV from HBM."""
+    n = len(step.copies)
+    whole = capture(lambda: [(step.segment(i % n), step.merge(i % n)) for i in range(steps)])
+    step_us = time_graph(whole, steps, warmup, world)
+    seg = capture(lambda: [step.segment(i % n) for i in range(steps)])
+    seg_us = time_graph(seg, steps, warmup, world)
+    merge = capture(lambda: [step.merge(i % n) for i in range(steps)])
+    merge_us = time_graph(merge, steps, warmup, world)
+    del whole, seg, merge
+    return step_us, seg_us, merge_us
+
+
+def time_e2e(q_host, step, steps, warmup, world):
     """Public-API step with host buffers: H2D of the queries, attention_matrix, D2H of the output."""
     out_host = torch.empty(step.p.out.shape, dtype=step.p.out.dtype, pin_memory=True)
-    q_dev = step.q
+    n = len(step.copies)
 
-    def one():
+    def one(i):
+        q_dev, kp, vp = step.copies[i % n]
         q_dev.copy_(q_host, non_blocking=True)
-        out = kernels.attention_matrix(q_dev, step.kp, step.vp, step.p)
+        out = kernels.attention_matrix(q_dev, kp, vp, step.p)
         out_host.copy_(out, non_blocking=True)
 
-    for _ in range(warmup):
-        flush.zero_()
-        one()
+    for i in range(warmup):
+        one(i)
     barrier(world)
     pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    for e0, e1 in pairs:
-        flush.zero_()
+    for i, (e0, e1) in enumerate(pairs):
         e0.record()
-        one()
+        one(i)
         e1.record()
     barrier(world)
     us = sum(a.elapsed_time(b) for a, b in pairs) * 1e3 / steps
@@ -299,7 +303,7 @@ def run_b200(args):
     tree = headline_tree()
     dev = torch.device("cuda", local)
     q, kp, vp = make_inputs(tree, heads, dev)
-    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    copies = [(q, kp, vp)] + [(q.clone(), kp.clone(), vp.clone()) for _ in range(COPIES - 1)]
     model = CostModel.b200()
 
     results = {}
@@ -310,19 +314,19 @@ def run_b200(args):
     prepared = kernels.prepare(plan, q, num_kv_heads=len(heads))
     torch.cuda.synchronize()
     metadata_us = (time.perf_counter() - t0) * 1e6
-    step = Step(q, kp, vp, prepared)
+    step = Step(copies, prepared)
 
     sampler = ClockSampler(local)
     sampler.start()
     burn_end = time.perf_counter() + (0.0 if args.quick else args.burn_s)
+    i = 0
     while time.perf_counter() < burn_end:       # sustained load so the clock samples see the step
-        flush.zero_()
-        step.segment()
-        step.merge()
-    seg_us, merge_us = time_step(step, args.steps, args.warmup, flush, world)
+        step.segment(i % COPIES)
+        step.merge(i % COPIES)
+        i += 1
+    step_us_local, seg_us, merge_us = time_step(step, args.steps, args.warmup, world)
     clocks = sampler.stop()
     kernels.check_status(prepared)
-    step_us_local = seg_us + merge_us
     step_us = max_over_ranks(step_us_local, world)
     seg_us_max = max_over_ranks(seg_us, world)
 
@@ -331,12 +335,12 @@ def run_b200(args):
         if args.quick or (not args.all_plans and method != "request"):
             continue
         pl = kernels.prepare(schedule(tree, HQ, HK, D, method, m), q, num_kv_heads=len(heads))
-        s, mg = time_step(Step(q, kp, vp, pl), max(3, args.steps // 2), args.warmup, flush, world)
-        results[method] = {"step_us": max_over_ranks(s + mg, world), "jobs": len(pl.jobs)}
+        whole, _, _ = time_step(Step(copies, pl), max(3, args.steps // 2), args.warmup, world)
+        results[method] = {"step_us": max_over_ranks(whole, world), "jobs": len(pl.jobs)}
         del pl
 
     q_host = q.cpu().pin_memory()
-    e2e_us, h2d, d2h = time_e2e(q_host, step, 1 if args.quick else args.steps, args.warmup, flush, world)
+    e2e_us, h2d, d2h = time_e2e(q_host, step, 1 if args.quick else args.steps, args.warmup, world)
     e2e_us = max_over_ranks(e2e_us, world)
     kernels.check_status(prepared)
 
@@ -355,8 +359,9 @@ def run_b200(args):
                    "plan": args.method, "cost_model": "CostModel.b200()", "jobs": len(prepared.jobs),
                    "physical_kv_bytes": total_bytes, "logical_kv_bytes": sum(len(p) for p in tree.paths) * HK * D * 4,
                    "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
-                   "l2": "512 MB buffer overwritten between timed steps (KV set 66.8 MB < 126 MB L2)",
-                   "timing": "CUDA events per step around CUDA-graph replays of the segment and merge launches",
+                   "l2": f"inputs larger than L2: steps rotate through {COPIES} copies of Q/K/V "
+                         f"({COPIES} x {kv_bytes(tree, len(heads)) / 1e6:.1f} MB)",
+                   "timing": "CUDA events around one CUDA-graph replay of K consecutive steps",
                    "plan_us": round(plan_us, 1), "metadata_us": round(metadata_us, 1)},
         "segment_us": round(seg_us_max, 3), "merge_us": round(max_over_ranks(merge_us, world), 3),
         "e2e": {"value": round(total_bytes / (e2e_us * 1e-6) / 1e9, 2), "unit": "GB/s", "step_us": round(e2e_us, 3),

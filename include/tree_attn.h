@@ -49,7 +49,7 @@
 extern "C" {
 #endif
 
-#define TA_ABI_VERSION 1
+#define TA_ABI_VERSION 2
 
 #define TA_DTYPE_BF16 1
 #define TA_DTYPE_F16 2
@@ -72,6 +72,9 @@ typedef struct ta_plan_layout {
   /* small tasks are sorted by padded row count: [0, e0) need 4 rows,
      [e0, e1) 8 rows, [e1, e2) 16 rows; e2 == num_small_tasks */
   int32_t small_class_end[3];
+  /* longest segment among small tasks when the plan was built (a hint: the
+     SIMT kernel single-buffers when every task fits one 64-key chunk) */
+  int32_t small_max_keys;
   int32_t kstart_stride;
   int32_t off_qids;
   int32_t off_kstart;

@@ -91,7 +91,7 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
   cudaError_t err = cudaSuccess;
   if (plan->num_tc_tasks > 0) err = launch_seg_tc(p, plan->num_tc_tasks, dtype, s);
   if (err == cudaSuccess && plan->num_small_tasks > 0)
-    err = launch_seg_simt(p, plan->small_class_end, head_dim, dtype, s);
+    err = launch_seg_simt(p, plan->small_class_end, plan->small_max_keys, head_dim, dtype, s);
   return launch_status(err);
 }
 

@@ -50,7 +50,9 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) 
     m = fmaxf(m, warp_max(l));
   }
 
-  // pass 2: weights exp(lse - m) and the weighted sum of partial rows
+  // pass 2: weights exp(lse - m) and the weighted sum of partial rows; lane k
+  // owns the weight and row offset of partial k0 + k, and the rows are read
+  // four at a time so their loads overlap.
   float acc[DL];
 #pragma unroll
   for (int e = 0; e < DL; ++e) acc[e] = 0.f;
@@ -58,29 +60,43 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) 
   if (m != -INFINITY) {
     for (int k0 = 0; k0 < count; k0 += 32) {
       float w = 0.f;
-      bool ok = false;
+      int64_t row = 0;
       if (k0 + lane < count) {
-        const int64_t row = row_of(k0 + lane, ok);
+        bool ok;
+        row = row_of(k0 + lane, ok);
         if (ok) w = fast_exp2((p.lse[row] - m) * kLog2e);  // -inf lse gives 0
       }
       z += warp_sum(w);
       const int n = min(32, count - k0);
-      for (int j = 0; j < n; ++j) {
-        const float wj = __shfl_sync(0xffffffffu, w, j);
-        if (wj == 0.f) continue;  // empty partial: its row may hold anything
-        bool okj;
-        const int64_t row = row_of(k0 + j, okj);
-        const float* src = p.part + row * D + lane * DL;
-        if constexpr (DL == 4) {
-          const float4 x = *reinterpret_cast<const float4*>(src);
-          acc[0] = fmaf(wj, x.x, acc[0]); acc[1] = fmaf(wj, x.y, acc[1]);
-          acc[2] = fmaf(wj, x.z, acc[2]); acc[3] = fmaf(wj, x.w, acc[3]);
-        } else if constexpr (DL == 2) {
-          const float2 x = *reinterpret_cast<const float2*>(src);
-          acc[0] = fmaf(wj, x.x, acc[0]); acc[1] = fmaf(wj, x.y, acc[1]);
-        } else {
-          acc[0] = fmaf(wj, src[0], acc[0]);
+      for (int j = 0; j < n; j += 4) {
+        float wj[4];
+        float x[4][DL];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int src = min(j + u, n - 1);
+          wj[u] = __shfl_sync(0xffffffffu, w, src);
+          const int64_t rj = __shfl_sync(0xffffffffu, row, src);
+          if (j + u >= n) wj[u] = 0.f;
+          // an empty partial (weight 0) may hold anything: do not read it
+          const float* ptr = p.part + rj * D + lane * DL;
+#pragma unroll
+          for (int e = 0; e < DL; ++e) x[u][e] = 0.f;
+          if (wj[u] != 0.f) {
+            if constexpr (DL == 4) {
+              const float4 v = *reinterpret_cast<const float4*>(ptr);
+              x[u][0] = v.x; x[u][1] = v.y; x[u][2] = v.z; x[u][3] = v.w;
+            } else if constexpr (DL == 2) {
+              const float2 v = *reinterpret_cast<const float2*>(ptr);
+              x[u][0] = v.x; x[u][1] = v.y;
+            } else {
+              x[u][0] = ptr[0];
+            }
+          }
         }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int e = 0; e < DL; ++e) acc[e] = fmaf(wj[u], x[u][e], acc[e]);
       }
     }
   }

@@ -2,15 +2,19 @@
 //
 // Work of one CTA: one (job, 16-row tile, KV head).  The job's key rows are a
 // contiguous run of the token-major pool, so each 64-key chunk of K and of V is
-// ONE 1-D bulk copy (cp.async.bulk, no multicast) into shared memory, double
-// buffered on two mbarriers.  The arithmetic is HBM-bound (4 rows x 128 dims
-// per 512 bytes of KV for a private request), so it stays on the FP32 pipe:
+// ONE 1-D bulk copy (cp.async.bulk, no multicast) into shared memory.  The
+// arithmetic is HBM-bound (4 rows x 128 dims per 512 bytes of KV for a private
+// request), so it stays on the FP32 pipe, and every warp runs its own online
+// softmax over its quarter of each chunk -- no CTA-wide barrier per chunk:
 //   scores   lanes split head_dim; a warp transpose-reduction turns 32 lane
-//            partials into 32 (row, key) dot products with 31 shuffles;
-//   softmax  per row over the chunk, exp2 on pre-scaled scores, running max /
-//            denominator in shared memory (online softmax across chunks);
-//   P.V      lanes split head_dim; each warp accumulates its keys, the four
-//            warps are summed once at the end.
+//            partials into 32 (key, row) dot products with 31 shuffles
+//   softmax  row max / sum over the warp's keys by shuffles within the lanes
+//            that hold the same row; exp2 on pre-scaled scores
+//   P.V      lanes split head_dim; p broadcast by shuffles
+// The four warps' (max, sum, accumulator) are merged once at the end with the
+// same log-sum-exp rule as the global merge.  Chunks live in STAGES shared
+// buffers (one when every task fits one chunk, two otherwise), refilled by
+// thread 0 once all warps have released the buffer on its EMPTY mbarrier.
 // Output: softmax-normalised partial O (f32) and natural-log LSE per row, as
 // the reference's _segment kernel (kernels.py:8-55) writes them.
 #include "ta_common.cuh"
@@ -22,24 +26,17 @@ namespace {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kChunk = 64;           // keys per chunk
+constexpr int kChunk = 64;                 // keys per chunk
 constexpr int kKeysPerWarp = kChunk / kWarps;
-constexpr int kStages = 2;
 
-template <int D, int R>
+template <int D, int R, int STAGES>
 struct SimtSmem {
-  static constexpr int kSPitch = kChunk + 4;
-  static constexpr size_t kv_bytes = size_t(kStages) * kChunk * D * 2;  // one of K / V
-  static constexpr size_t off_k = 0;
-  static constexpr size_t off_v = off_k + kv_bytes;
-  static constexpr size_t off_s = off_v + kv_bytes;                    // [R][kSPitch] f32
-  static constexpr size_t off_p = off_s + size_t(R) * kSPitch * 4;     // [kChunk][R] f32
-  static constexpr size_t off_m = off_p + size_t(kChunk) * R * 4;      // [R] running max (log2)
-  static constexpr size_t off_z = off_m + R * 4;                       // [R] denominators
-  static constexpr size_t off_a = off_z + R * 4;                       // [R] chunk rescale
-  static constexpr size_t off_bar = (off_a + R * 4 + 15) / 16 * 16;    // [kStages] mbarriers
-  static constexpr size_t bytes = off_bar + kStages * 8;
-  static_assert(size_t(kWarps) * R * D * 4 <= 2 * kv_bytes, "final reduction reuses the KV buffers");
+  static constexpr size_t stage_bytes = size_t(kChunk) * D * 2 * 2;   // K and V of one chunk
+  static constexpr size_t off_stage = 0;
+  static constexpr size_t off_mz = off_stage + STAGES * stage_bytes;   // [4 warps][R] max, then sum
+  static constexpr size_t off_bar = (off_mz + 2 * kWarps * R * 4 + 15) / 16 * 16;
+  static constexpr size_t bytes = off_bar + 2 * STAGES * 8;
+  static_assert(size_t(kWarps) * R * D * 4 <= STAGES * stage_bytes, "warp combine reuses the chunk buffers");
 };
 
 template <typename T, int D>
@@ -57,22 +54,18 @@ __device__ __forceinline__ void load_slice(const uint16_t* base, float (&x)[D / 
   }
 }
 
-template <typename T, int D, int R>
+template <typename T, int D, int R, int STAGES>
 __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int task_begin) {
-  using L = SimtSmem<D, R>;
+  using L = SimtSmem<D, R, STAGES>;
   constexpr int DL = D / 32;
-  constexpr int KB = 32 / R;                  // keys per transpose-reduction batch
+  constexpr int KB = 32 / R;                           // keys per transpose-reduction batch
+  constexpr int NB = kKeysPerWarp / KB;                // batches per warp and chunk
   static_assert(32 % R == 0 && kKeysPerWarp % KB == 0, "row padding must divide the warp");
 
   extern __shared__ __align__(128) unsigned char smem[];
-  uint16_t* k_s = reinterpret_cast<uint16_t*>(smem + L::off_k);
-  uint16_t* v_s = reinterpret_cast<uint16_t*>(smem + L::off_v);
-  float* s_s = reinterpret_cast<float*>(smem + L::off_s);
-  float* p_s = reinterpret_cast<float*>(smem + L::off_p);
-  float* m_s = reinterpret_cast<float*>(smem + L::off_m);
-  float* z_s = reinterpret_cast<float*>(smem + L::off_z);
-  float* a_s = reinterpret_cast<float*>(smem + L::off_a);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::off_bar);
+  uint64_t* empty = full + STAGES;
+  float* mz = reinterpret_cast<float*>(smem + L::off_mz);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int task = task_begin + blockIdx.x;
@@ -91,12 +84,34 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
   const int r0 = tile * 16;
   const int rows = min(R, nr * G - r0);
   const int64_t part_row0 = int64_t(p.slot_base[job]) * G + r0;
-  bool bad = nr < 0 || nr > p.max_requests || rows <= 0 || nk < 0 || k0 < 0 || k0 + nk > p.pool_tokens ||
-             part_row0 < 0 || part_row0 + rows > int64_t(p.num_partials) * G;
-  if (bad) {
+  const bool rows_ok = rows > 0 && part_row0 >= 0 && part_row0 + rows <= int64_t(p.num_partials) * G;
+  if (!rows_ok || nr > p.max_requests || nk < 0 || k0 < 0 || k0 + nk > p.pool_tokens) {
     if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
-    if (rows <= 0 || part_row0 < 0 || part_row0 + rows > int64_t(p.num_partials) * G) return;
+    if (!rows_ok) return;
     nk = 0;  // rows are addressable: publish an empty partial (O = 0, LSE = -inf)
+  }
+  const int nchunks = (nk + kChunk - 1) / kChunk;
+  const uint16_t* kbase = p.k + (int64_t(head) * p.pool_tokens + k0) * D;
+  const uint16_t* vbase = p.v + (int64_t(head) * p.pool_tokens + k0) * D;
+  auto stage_k = [&](int s) { return reinterpret_cast<uint16_t*>(smem + L::off_stage + s * L::stage_bytes); };
+  auto stage_v = [&](int s) { return stage_k(s) + kChunk * D; };
+  auto issue = [&](int c) {
+    const int keys = min(kChunk, nk - c * kChunk);
+    const uint32_t bytes = uint32_t(keys) * D * 2;
+    const int st = c % STAGES;
+    mbar_arrive_expect_tx(&full[st], 2 * bytes);
+    bulk_g2s(stage_k(st), kbase + int64_t(c) * kChunk * D, bytes, &full[st]);
+    bulk_g2s(stage_v(st), vbase + int64_t(c) * kChunk * D, bytes, &full[st]);
+  };
+
+  // Thread 0 starts the KV stream before anything else.
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    fence_barrier_init();
+    for (int c = 0; c < min(nchunks, STAGES); ++c) issue(c);
   }
 
   // Query slice of every row, pre-scaled into the log2 domain.
@@ -118,32 +133,10 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
       }
     }
   }
+  __syncthreads();  // barrier initialisation is visible to every warp
 
-  if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
-    fence_barrier_init();
-  }
-  if (tid < R) {
-    m_s[tid] = -INFINITY;
-    z_s[tid] = 0.f;
-  }
-  __syncthreads();
-
-  const int nchunks = (nk + kChunk - 1) / kChunk;
-  const uint16_t* kbase = p.k + (int64_t(head) * p.pool_tokens + k0) * D;
-  const uint16_t* vbase = p.v + (int64_t(head) * p.pool_tokens + k0) * D;
-  auto issue = [&](int c) {
-    const int keys = min(kChunk, nk - c * kChunk);
-    const uint32_t bytes = uint32_t(keys) * D * 2;
-    const int st = c % kStages;
-    mbar_arrive_expect_tx(&bars[st], 2 * bytes);
-    bulk_g2s(k_s + size_t(st) * kChunk * D, kbase + int64_t(c) * kChunk * D, bytes, &bars[st]);
-    bulk_g2s(v_s + size_t(st) * kChunk * D, vbase + int64_t(c) * kChunk * D, bytes, &bars[st]);
-  };
-  if (tid == 0) {
-    for (int c = 0; c < min(nchunks, kStages); ++c) issue(c);
-  }
-
+  // Per-warp online softmax state.  Lane l holds the state of row l % R.
+  float m_run = -INFINITY, z_run = 0.f;
   float acc[R][DL];
 #pragma unroll
   for (int r = 0; r < R; ++r)
@@ -152,20 +145,19 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
 
   bool alive = true;
   for (int c = 0; c < nchunks; ++c) {
-    const int st = c % kStages;
+    const int st = c % STAGES;
     const int keys = min(kChunk, nk - c * kChunk);
-    if (!mbar_wait(&bars[st], (c / kStages) & 1, p.status)) alive = false;
-    if (__syncthreads_or(!alive)) {
-      alive = false;
-      break;
-    }
-    const uint16_t* kc = k_s + size_t(st) * kChunk * D;
-    const uint16_t* vc = v_s + size_t(st) * kChunk * D;
+    alive = __all_sync(0xffffffffu, mbar_wait(&full[st], (c / STAGES) & 1, p.status));
+    if (!alive) break;
+    const uint16_t* kc = stage_k(st);
+    const uint16_t* vc = stage_v(st);
+    const int kw = warp * kKeysPerWarp;                  // this warp's first key in the chunk
 
-    // -- scores: warp `warp` owns keys [16*warp, 16*warp + 16) of the chunk
+    // -- scores of this warp's 16 keys: s[b] for key kw + b*KB + lane/R, row lane%R
+    float s[NB];
 #pragma unroll
-    for (int b = 0; b < kKeysPerWarp / KB; ++b) {
-      const int kb = warp * kKeysPerWarp + b * KB;
+    for (int b = 0; b < NB; ++b) {
+      const int kb = kw + b * KB;
       float part[32];
 #pragma unroll
       for (int kk = 0; kk < KB; ++kk) {
@@ -173,98 +165,118 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
         load_slice<T, D>(kc + (kb + kk) * D + lane * DL, kx);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          float s = 0.f;
+          float acc_s = 0.f;
 #pragma unroll
-          for (int e = 0; e < DL; ++e) s = fmaf(qr[r][e], kx[e], s);
-          part[kk * R + r] = s;
+          for (int e = 0; e < DL; ++e) acc_s = fmaf(qr[r][e], kx[e], acc_s);
+          part[kk * R + r] = acc_s;
         }
       }
       const float dot = warp_transpose_sum32(part, lane);
-      const int key = kb + lane / R, r = lane % R;
-      s_s[r * L::kSPitch + key] = key < keys ? dot : -INFINITY;
+      s[b] = (kb + lane / R < keys) ? dot : -INFINITY;
     }
-    __syncthreads();
 
-    // -- online softmax, one warp per row (rows warp, warp+4, ...)
-    for (int r = warp; r < R; r += kWarps) {
-      const float s0 = s_s[r * L::kSPitch + lane];
-      const float s1 = s_s[r * L::kSPitch + lane + 32];
-      const float m_old = m_s[r];
-      const float m_new = fmaxf(m_old, warp_max(fmaxf(s0, s1)));
-      const float base = m_new == -INFINITY ? 0.f : m_new;
-      const float p0 = fast_exp2(s0 - base), p1 = fast_exp2(s1 - base);
-      p_s[lane * R + r] = p0;
-      p_s[(lane + 32) * R + r] = p1;
-      const float sum = warp_sum(p0 + p1);
-      if (lane == 0) {
-        const float alpha = fast_exp2(m_old - base);  // m_old = -inf gives 0
-        a_s[r] = alpha;
-        z_s[r] = z_s[r] * alpha + sum;
-        m_s[r] = m_new;
-      }
+    // -- row max / sum within the lanes holding the same row (lane % R)
+    float mx = s[0];
+#pragma unroll
+    for (int b = 1; b < NB; ++b) mx = fmaxf(mx, s[b]);
+#pragma unroll
+    for (int off = R; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const float m_new = fmaxf(m_run, mx);
+    const float base = m_new == -INFINITY ? 0.f : m_new;
+    const float alpha = fast_exp2(m_run - base);          // m_run = -inf gives 0
+    float sum = 0.f;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      s[b] = fast_exp2(s[b] - base);                       // now p
+      sum += s[b];
     }
-    __syncthreads();
+#pragma unroll
+    for (int off = R; off < 32; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    z_run = z_run * alpha + sum;
+    m_run = m_new;
 
-    // -- P.V: warp owns the same 16 keys, lanes split head_dim
+    // -- P.V over this warp's keys; lanes split head_dim
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      const float alpha = a_s[r];
+      const float a_r = __shfl_sync(0xffffffffu, alpha, r);
 #pragma unroll
-      for (int e = 0; e < DL; ++e) acc[r][e] *= alpha;
+      for (int e = 0; e < DL; ++e) acc[r][e] *= a_r;
     }
-    const int kend = min(keys, (warp + 1) * kKeysPerWarp);
-    for (int key = warp * kKeysPerWarp; key < kend; ++key) {
-      float vx[DL];
-      load_slice<T, D>(vc + key * D + lane * DL, vx);
-      const float4* prow = reinterpret_cast<const float4*>(p_s + key * R);
 #pragma unroll
-      for (int r4 = 0; r4 < R / 4; ++r4) {
-        const float4 pv = prow[r4];
-        const float pr[4] = {pv.x, pv.y, pv.z, pv.w};
+    for (int b = 0; b < NB; ++b) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+      for (int kk = 0; kk < KB; ++kk) {
+        const int key = kw + b * KB + kk;
+        if (key < keys) {                                  // warp-uniform
+          float vx[DL];
+          load_slice<T, D>(vc + key * D + lane * DL, vx);
 #pragma unroll
-          for (int e = 0; e < DL; ++e) acc[r4 * 4 + j][e] = fmaf(pr[j], vx[e], acc[r4 * 4 + j][e]);
+          for (int r = 0; r < R; ++r) {
+            const float pr = __shfl_sync(0xffffffffu, s[b], kk * R + r);
+#pragma unroll
+            for (int e = 0; e < DL; ++e) acc[r][e] = fmaf(pr, vx[e], acc[r][e]);
+          }
+        }
       }
     }
-    __syncthreads();  // stage `st` and s_s / p_s are free again
-    if (tid == 0 && c + kStages < nchunks) issue(c + kStages);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (tid == 0 && c + STAGES < nchunks) {
+      // refill this buffer once every warp has released it
+      if (mbar_wait(&empty[st], (c / STAGES) & 1, p.status)) issue(c + STAGES);
+    }
   }
 
-  // -- sum the four warps' accumulators (reusing the KV buffers) and publish
-  float* red = reinterpret_cast<float*>(smem + L::off_k);
-  if (alive) {
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-      for (int e = 0; e < DL; ++e) red[(warp * R + r) * D + lane * DL + e] = acc[r][e];
+  // -- combine the four warps (reusing the chunk buffers: every issued chunk
+  // has been consumed, so no copy is in flight) and publish
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(smem + L::off_stage);
+  if (lane < R) {
+    mz[warp * R + lane] = alive ? m_run : -INFINITY;
+    mz[kWarps * R + warp * R + lane] = alive ? z_run : 0.f;
   }
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int e = 0; e < DL; ++e) red[(warp * R + r) * D + lane * DL + e] = acc[r][e];
   __syncthreads();
   for (int i = tid; i < rows * D; i += kThreads) {
     const int r = i / D, d = i % D;
-    float o = 0.f;
-    const float z = z_s[r];
-    if (alive && z > 0.f) {
-      o = red[(0 * R + r) * D + d] + red[(1 * R + r) * D + d] + red[(2 * R + r) * D + d] +
-          red[(3 * R + r) * D + d];
-      o /= z;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mz[w * R + r]);
+    float o = 0.f, zt = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float wgt = fast_exp2(mz[w * R + r] - M);   // -inf max (no keys) gives 0
+        o = fmaf(wgt, red[(w * R + r) * D + d], o);
+        zt = fmaf(wgt, mz[kWarps * R + w * R + r], zt);
+      }
     }
-    p.part[(int64_t(head) * p.num_partials * G + part_row0 + r) * D + d] = o;
+    p.part[(int64_t(head) * p.num_partials * G + part_row0 + r) * D + d] = zt > 0.f ? o / zt : 0.f;
   }
   if (tid < rows) {
-    const float z = z_s[tid];
-    const float l = (alive && z > 0.f) ? (m_s[tid] + fast_log2(z)) * kLn2 : -INFINITY;
-    p.lse[int64_t(head) * p.num_partials * G + part_row0 + tid] = l;
+    const int r = tid;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mz[w * R + r]);
+    float zt = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) zt = fmaf(fast_exp2(mz[w * R + r] - M), mz[kWarps * R + w * R + r], zt);
+    }
+    p.lse[int64_t(head) * p.num_partials * G + part_row0 + r] = zt > 0.f ? (M + fast_log2(zt)) * kLn2 : -INFINITY;
   }
 }
 
 }  // namespace
 
-template <typename T, int D, int R>
+template <typename T, int D, int R, int STAGES>
 static cudaError_t launch_simt_class(const SegParams& p, int begin, int count, cudaStream_t stream) {
   if (count <= 0) return cudaSuccess;
-  using L = SimtSmem<D, R>;
-  auto kernel = seg_simt_kernel<T, D, R>;
+  using L = SimtSmem<D, R, STAGES>;
+  auto kernel = seg_simt_kernel<T, D, R, STAGES>;
   static bool configured = false;  // the attribute is per function and persists
   if (!configured) {
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::bytes));
@@ -276,24 +288,34 @@ static cudaError_t launch_simt_class(const SegParams& p, int begin, int count, c
   return cudaGetLastError();
 }
 
-template <typename T, int D>
-static cudaError_t launch_simt_dim(const SegParams& p, const int32_t class_end[3], cudaStream_t stream) {
-  cudaError_t err = launch_simt_class<T, D, 4>(p, 0, class_end[0], stream);
-  if (err == cudaSuccess) err = launch_simt_class<T, D, 8>(p, class_end[0], class_end[1] - class_end[0], stream);
-  if (err == cudaSuccess) err = launch_simt_class<T, D, 16>(p, class_end[1], class_end[2] - class_end[1], stream);
+template <typename T, int D, int STAGES>
+static cudaError_t launch_simt_stages(const SegParams& p, const int32_t class_end[3], cudaStream_t stream) {
+  cudaError_t err = launch_simt_class<T, D, 4, STAGES>(p, 0, class_end[0], stream);
+  if (err == cudaSuccess)
+    err = launch_simt_class<T, D, 8, STAGES>(p, class_end[0], class_end[1] - class_end[0], stream);
+  if (err == cudaSuccess)
+    err = launch_simt_class<T, D, 16, STAGES>(p, class_end[1], class_end[2] - class_end[1], stream);
   return err;
 }
 
-cudaError_t launch_seg_simt(const SegParams& p, const int32_t class_end[3], int head_dim, int dtype,
+template <typename T, int D>
+static cudaError_t launch_simt_dim(const SegParams& p, const int32_t class_end[3], int max_keys, cudaStream_t stream) {
+  // One buffer suffices when every task fits one chunk (leaves, short tails);
+  // longer tasks double-buffer so the next chunk streams during compute.
+  if (max_keys <= kChunk) return launch_simt_stages<T, D, 1>(p, class_end, stream);
+  return launch_simt_stages<T, D, 2>(p, class_end, stream);
+}
+
+cudaError_t launch_seg_simt(const SegParams& p, const int32_t class_end[3], int max_keys, int head_dim, int dtype,
                             cudaStream_t stream) {
   if (dtype == TA_DTYPE_BF16) {
-    if (head_dim == 128) return launch_simt_dim<__nv_bfloat16, 128>(p, class_end, stream);
-    if (head_dim == 64) return launch_simt_dim<__nv_bfloat16, 64>(p, class_end, stream);
-    if (head_dim == 32) return launch_simt_dim<__nv_bfloat16, 32>(p, class_end, stream);
+    if (head_dim == 128) return launch_simt_dim<__nv_bfloat16, 128>(p, class_end, max_keys, stream);
+    if (head_dim == 64) return launch_simt_dim<__nv_bfloat16, 64>(p, class_end, max_keys, stream);
+    if (head_dim == 32) return launch_simt_dim<__nv_bfloat16, 32>(p, class_end, max_keys, stream);
   } else if (dtype == TA_DTYPE_F16) {
-    if (head_dim == 128) return launch_simt_dim<__half, 128>(p, class_end, stream);
-    if (head_dim == 64) return launch_simt_dim<__half, 64>(p, class_end, stream);
-    if (head_dim == 32) return launch_simt_dim<__half, 32>(p, class_end, stream);
+    if (head_dim == 128) return launch_simt_dim<__half, 128>(p, class_end, max_keys, stream);
+    if (head_dim == 64) return launch_simt_dim<__half, 64>(p, class_end, max_keys, stream);
+    if (head_dim == 32) return launch_simt_dim<__half, 32>(p, class_end, max_keys, stream);
   }
   return cudaErrorInvalidValue;
 }

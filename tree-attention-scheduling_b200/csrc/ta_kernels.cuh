@@ -38,7 +38,7 @@ struct MergeParams {
   int32_t num_requests, max_slots, num_partials, num_q_heads, group;
 };
 
-cudaError_t launch_seg_simt(const SegParams& p, const int32_t class_end[3], int head_dim, int dtype,
+cudaError_t launch_seg_simt(const SegParams& p, const int32_t class_end[3], int max_keys, int head_dim, int dtype,
                             cudaStream_t stream);
 cudaError_t launch_seg_tc(const SegParams& p, int num_tasks, int dtype, cudaStream_t stream);
 cudaError_t launch_merge(const MergeParams& p, int head_dim, int dtype, cudaStream_t stream);

@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libtree_attn_b200.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 DTYPE_BF16 = 1
 DTYPE_F16 = 2
@@ -43,6 +43,7 @@ class PlanLayout(ctypes.Structure):
         ("num_small_tasks", ctypes.c_int32),
         ("num_tc_tasks", ctypes.c_int32),
         ("small_class_end", ctypes.c_int32 * 3),
+        ("small_max_keys", ctypes.c_int32),
         ("kstart_stride", ctypes.c_int32),
         ("off_qids", ctypes.c_int32),
         ("off_kstart", ctypes.c_int32),

@@ -136,11 +136,12 @@ def build_metadata(jobs, num_requests, groups, use_tc):
             for t in range(ceil(rows / SMALL_ROWS)):
                 small[_small_class(min(SMALL_ROWS, rows - t * SMALL_ROWS))].append((i, t))
     class_end = np.cumsum([len(c) for c in small]).astype(np.int32)
+    small_max_keys = max((int(klen[i]) for c in small for i, _ in c), default=0)
     small_tasks = np.array([t for c in small for t in c], dtype=np.int32).reshape(-1, 2)
     tc_tasks = np.array(tc, dtype=np.int32).reshape(-1, 2)
     return dict(qids=qids, kids=kids, qlen=qlen, klen=klen, slots=slots, counts=counts,
                 slot_base=slot_base, cslots=cslots, small_tasks=small_tasks, tc_tasks=tc_tasks,
-                small_class_end=class_end, contiguous_k=contiguous_k,
+                small_class_end=class_end, small_max_keys=small_max_keys, contiguous_k=contiguous_k,
                 num_partials=int(qlen.sum()))
 
 
@@ -193,6 +194,7 @@ def prepare(plan, q, num_kv_heads=None):
     layout.num_tc_tasks = meta["tc_tasks"].shape[0]
     for i in range(3):
         layout.small_class_end[i] = int(meta["small_class_end"][i])
+    layout.small_max_keys = meta["small_max_keys"]
     layout.kstart_stride = meta["kids"].shape[1]
     layout.off_qids = offsets["qids"]
     layout.off_kstart = offsets["kids"]
