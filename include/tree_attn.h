@@ -60,6 +60,10 @@ extern "C" {
 #define TA_ERR_BOUNDS 4       /* device: plan index out of range, access skipped */
 #define TA_ERR_TIMEOUT 8      /* device: a bounded wait gave up */
 #define TA_ERR_UNSUPPORTED 16 /* host: shape or dtype without a kernel */
+#define TA_ERR_TOO_LARGE 32   /* host: the problem exceeds ta_attention_noalloc's fixed scratch */
+
+/* Size of the device scratch array behind ta_attention_noalloc, per GPU. */
+#define TA_NOALLOC_SCRATCH_BYTES (32u << 20)
 
 typedef struct ta_plan_layout {
   int32_t num_jobs;
@@ -125,6 +129,25 @@ int ta_attention(const ta_plan_layout* plan, const int32_t* meta, const void* q,
                  const void* vpool, int64_t pool_tokens, int32_t num_q_heads, int32_t num_kv_heads,
                  int32_t head_dim, int32_t dtype, float* part, float* lse, void* out, float* out_lse,
                  int32_t* status, void* stream);
+
+/*
+ * ta_attention for callers that cannot allocate device memory: no counterpart
+ * in the reference, which always allocates its scratch in prepare().  A host
+ * that captures its decode step into a CUDA graph in global capture mode, a
+ * process whose device memory is owned by another allocator, or a binding
+ * without access to a CUDA allocator passes only its inputs and outputs; the
+ * partial outputs and LSEs live in one file-scope device array of
+ * TA_NOALLOC_SCRATCH_BYTES per GPU (held by every GPU that loads the library,
+ * until exit).  Problems needing more than that -- num_kv_heads * num_partials
+ * * G * (head_dim + 1) floats plus 256 bytes -- return TA_ERR_TOO_LARGE without
+ * launching.  The first call on a device looks the array's address up (make it
+ * before any stream capture).  All calls share the array: calls whose kernels
+ * overlap on the GPU race on it and must be serialised by the caller; nothing
+ * in it needs to start at zero.  Allocates nothing.
+ */
+int ta_attention_noalloc(const ta_plan_layout* plan, const int32_t* meta, const void* q, const void* kpool,
+                         const void* vpool, int64_t pool_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                         int32_t head_dim, int32_t dtype, void* out, float* out_lse, int32_t* status, void* stream);
 
 /*
  * klen[tail_jobs[i]] = value for i < num_tails, on the device: the per-step

@@ -21,15 +21,18 @@ ERR_LAUNCH = 2
 ERR_BOUNDS = 4
 ERR_TIMEOUT = 8
 ERR_UNSUPPORTED = 16
+ERR_TOO_LARGE = 32
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 STATUS_NAMES = {ERR_ARG: "invalid argument", ERR_LAUNCH: "kernel launch failed",
                 ERR_BOUNDS: "plan index out of range on the device",
                 ERR_TIMEOUT: "bounded device wait gave up",
-                ERR_UNSUPPORTED: "shape or dtype not supported"}
+                ERR_UNSUPPORTED: "shape or dtype not supported",
+                ERR_TOO_LARGE: "problem exceeds the fixed no-allocation scratch"}
 
 # Every symbol declared in include/tree_attn.h.
 EXPORTS = ("ta_abi_version", "ta_error_string", "ta_segment", "ta_merge", "ta_attention",
-           "ta_update_tail_klen")
+           "ta_attention_noalloc", "ta_update_tail_klen")
 
 
 class PlanLayout(ctypes.Structure):
@@ -89,6 +92,8 @@ def load():
     lib.ta_merge.argtypes = [LP, P, P, P, P, P, I32, I32, I32, I32, P, P]
     lib.ta_attention.restype = ctypes.c_int
     lib.ta_attention.argtypes = [LP, P, P, P, P, I64, I32, I32, I32, I32, P, P, P, P, P, P]
+    lib.ta_attention_noalloc.restype = ctypes.c_int
+    lib.ta_attention_noalloc.argtypes = [LP, P, P, P, P, I64, I32, I32, I32, I32, P, P, P, P]
     lib.ta_update_tail_klen.restype = ctypes.c_int
     lib.ta_update_tail_klen.argtypes = [P, P, I32, I32, I32, P, P]
     version = lib.ta_abi_version()
