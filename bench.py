@@ -427,6 +427,131 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# Other BASELINE configurations (run explicitly; the default line is the headline)
+def random_inputs(tree, nreq, device, seed, copies=1):
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for _ in range(copies):
+        q = torch.randn(nreq, HQ, D, generator=g, device=device).bfloat16()
+        kp = torch.randn(HK, tree.storage_tokens, D, generator=g, device=device).bfloat16()
+        vp = torch.randn(HK, tree.storage_tokens, D, generator=g, device=device).bfloat16()
+        out.append((q, kp, vp))
+    return out
+
+
+def run_grid(args):
+    """81 seeded shapes, tree plan vs per-request plan on the same kernels."""
+    from tree_attention import workloads
+    import math
+    torch.cuda.set_device(0)
+    model = CostModel.b200()
+    rows = []
+    for params, tree in workloads.evaluation_grid(seed=args.seed or 201):
+        nreq = len(tree.paths)
+        kvb = kv_bytes(tree)
+        copies = max(1, min(8, math.ceil((256 << 20) / kvb)))
+        inputs = random_inputs(tree, nreq, "cuda", 201, copies)
+        row = dict(params, storage_tokens=tree.storage_tokens, logical_tokens=sum(map(len, tree.paths)))
+        for method in ("cube", "request"):
+            t0 = time.perf_counter()
+            plan = schedule(tree, HQ, HK, D, method, model)
+            plan_us = (time.perf_counter() - t0) * 1e6
+            prepared = kernels.prepare(plan, inputs[0][0])
+            step = Step(inputs, prepared)
+            whole, _, _ = time_step(step, args.steps, args.warmup, 1)
+            kernels.check_status(prepared)
+            row[method] = dict(step_us=round(whole, 2), plan_us=round(plan_us, 1), jobs=len(prepared.jobs))
+            del prepared, step
+        row["speedup"] = round(row["request"]["step_us"] / row["cube"]["step_us"], 4)
+        rows.append(row)
+        del inputs
+        torch.cuda.empty_cache()
+    speedups = [r["speedup"] for r in rows]
+    geo = math.exp(sum(math.log(x) for x in speedups) / len(speedups))
+    line = {"config": "grid (configs[2]): 81 shapes, requests {16,64,256} x depth {1,2,4} x shared "
+                      "{0.25,0.75,0.99} x branching {2,4,16}, context 2048-16384",
+            "metric": "geomean speed-up of the tree (cube) plan over the per-request plan, same kernels",
+            "value": round(geo, 4), "min": min(speedups), "max": max(speedups), "shapes": len(rows),
+            "steps": args.steps, "warmup": args.warmup, "cost_model": "CostModel.b200()", "rows": rows}
+    print(json.dumps(line), flush=True)
+
+
+def run_decode(args):
+    """a 32-request 2-level tree, 16 decode steps, plan reused vs rebuilt."""
+    from tree_attention import workloads
+    from tree_attention.kernels import CachedDecodePlan
+    from oracle import attention as oracle
+    import copy as _copy
+    torch.cuda.set_device(0)
+    steps = 16
+    base = workloads.decode_tree()
+    prefix = base.storage_tokens
+    nreq = len(base.paths)
+    g = torch.Generator(device="cuda").manual_seed(301)
+    q = torch.randn(nreq, HQ, D, generator=g, device="cuda").bfloat16()
+    kp = torch.randn(HK, prefix + nreq * steps, D, generator=g, device="cuda").bfloat16()
+    vp = torch.randn_like(kp)
+    model = CostModel.b200()
+    results = []
+
+    def device_us(fn, reps=10):
+        # reps back-to-back calls recorded in one CUDA graph: device time without launch gaps
+        graph = capture(lambda: [fn() for _ in range(reps)])
+        t = time_graph(graph, reps, 2, 1)
+        del graph
+        return t
+
+    def check(step, out):
+        paths = [path + tuple(prefix + r * steps + t for t in range(step + 1)) for r, path in enumerate(base.paths)]
+        sample = [0, nreq // 2, nreq - 1]
+        _, ref, _ = oracle.request_attention(q[sample].float().cpu(), kp.permute(1, 0, 2).float().cpu(),
+                                             vp.permute(1, 0, 2).float().cpu(), [paths[r] for r in sample],
+                                             return_lse=True)
+        err = ((out[sample].float().cpu() - ref).norm(dim=-1) / ref.norm(dim=-1)).max().item()
+        if err > 5e-3:
+            raise AssertionError(f"decode step {step}: rel L2 {err:.3e}")
+        return err
+
+    for method in ("fixed", "greedy", "cube"):
+        for mode in ("rebuild", "cached"):
+            tree = _copy.deepcopy(base)
+            leaves = list(range(len(base.nodes) - nreq, len(base.nodes)))
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            cached = CachedDecodePlan(schedule(tree, HQ, HK, D, method, model), q, prefix, steps) \
+                if mode == "cached" else None
+            torch.cuda.synchronize()
+            initial_us = (time.perf_counter() - t0) * 1e6
+            per_step, worst = [], 0.0
+            for step in range(steps):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                if mode == "rebuild":
+                    tree.extend_leaves(leaves, [prefix + r * steps + step for r in range(nreq)])
+                    p = kernels.prepare(schedule(tree, HQ, HK, D, method, model), q)
+                else:
+                    p = cached.update(step + 1)
+                torch.cuda.synchronize()
+                planning_us = (time.perf_counter() - t0) * 1e6
+                att_us = device_us(lambda: kernels.attention_matrix(q, kp, vp, p))
+                kernels.check_status(p)
+                if step in (0, steps - 1):
+                    worst = max(worst, check(step, kernels.attention_matrix(q, kp, vp, p).clone()))
+                per_step.append(dict(step=step + 1, planning_us=round(planning_us, 1), attention_us=round(att_us, 2)))
+            total = [s["planning_us"] + s["attention_us"] for s in per_step]
+            results.append(dict(method=method, mode=mode, initial_plan_us=round(initial_us, 1),
+                                planning_us=round(sum(s["planning_us"] for s in per_step) / steps, 1),
+                                attention_us=round(sum(s["attention_us"] for s in per_step) / steps, 2),
+                                per_step_us=round(sum(total) / steps, 1),
+                                amortized_us=round((initial_us + sum(total)) / steps, 1),
+                                max_rel_l2=worst))
+    line = {"config": "decode (configs[3]): 32 requests, 4096-token root, 4 x 1024 branches, 32 x 256 leaves, "
+                      "16 steps of 1 token per request", "metric": "planning + attention per step (us)",
+            "cost_model": "CostModel.b200()", "results": results}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -438,6 +563,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--burn-s", type=float, default=1.0, help="sustained untimed load before timing (clocks)")
+    ap.add_argument("--config", choices=["headline", "grid", "decode"], default="headline")
+    ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--quick", action="store_true",
                     help="main plan only: no burn, other plans, CPU baseline or repeated e2e (profiling runs)")
     args = ap.parse_args()
@@ -445,6 +572,10 @@ def main():
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "grid":
+        run_grid(args)
+    elif args.config == "decode":
+        run_decode(args)
     else:
         run_b200(args)
 

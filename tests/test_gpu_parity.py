@@ -255,3 +255,46 @@ def test_tensor_core_pipeline_tile_counts(keys, nreq):
     if nreq * 4 > kernels.SMALL_ROWS:
         assert p.layout.num_tc_tasks == (nreq * 4 + kernels.TC_ROWS - 1) // kernels.TC_ROWS
     check_against_oracle(q, k, v, tree.paths, out, lse)
+
+
+def test_evaluation_grid_sample_matches_oracle():
+    """A sample of the 81 evaluation-grid shapes (16 requests: every depth, shared
+    fraction and branching factor, uneven prefixes, internal terminations,
+    duplicates), tree and per-request plans against the FP32 oracle."""
+    from tree_attention import workloads
+    for index, (params, tree) in enumerate(workloads.evaluation_grid()):
+        if params["requests"] != 16 or params["context"] > 4096 or index % 2:
+            continue
+        q, k, v = make_inputs(16, tree.storage_tokens, 32, 8, 128, torch.bfloat16, seed=200 + index)
+        for method in ("cube", "request"):
+            plan = schedule(tree, 32, 8, 128, method, CostModel.b200())
+            out, lse, _ = run_kernel(q, k, v, plan, pool_pad=64)
+            check_against_oracle(q, k, v, tree.paths, out, lse)
+
+
+def test_decode_tree_plan_reuse_first_and_last_step():
+    """configs[3] shape: the cached plan and the rebuilt plan agree with the oracle
+    at the first and last of 16 decode steps."""
+    import copy
+    from tree_attention import workloads
+    steps = 16
+    base = workloads.decode_tree()
+    prefix = base.storage_tokens
+    q, k, v = make_inputs(32, prefix + 32 * steps, 32, 8, 128, torch.bfloat16, seed=301)
+    qd = q.cuda()
+    kp, vp = pack_kv(k.cuda(), v.cuda())
+    cached = CachedDecodePlan(schedule(base, 32, 8, 128, "cube", CostModel.b200()), qd, prefix, steps)
+    tree = copy.deepcopy(base)
+    leaves = list(range(len(base.nodes) - 32, len(base.nodes)))
+    for step in range(steps):
+        tree.extend_leaves(leaves, [prefix + r * steps + step for r in range(32)])
+        if step not in (0, steps - 1):
+            continue
+        paths = [path + tuple(prefix + r * steps + t for t in range(step + 1)) for r, path in enumerate(base.paths)]
+        assert [tuple(p) for p in tree.paths] == paths
+        for p in (cached.update(step + 1), prepare(schedule(tree, 32, 8, 128, "cube", CostModel.b200()), qd)):
+            lse = torch.empty(32, 32, device="cuda")
+            out = attention_matrix(qd, kp, vp, p, out_lse=lse).cpu()
+            torch.cuda.synchronize()
+            check_status(p)
+            check_against_oracle(q, k, v, paths, out, lse.cpu())
