@@ -195,7 +195,7 @@ class Step:
         self.lib = _lib.load()
         L = prepared.layout
         self.launches = (sum(1 for i, e in enumerate(L.small_class_end) if e > (L.small_class_end[i - 1] if i else 0))
-                         + (1 if L.num_tc_tasks else 0) + 1)
+                         + (1 if L.num_tc_tasks else 0) + (1 if L.num_kn_tasks else 0) + 1)
 
     def segment(self, copy=0):
         p = self.p

@@ -28,12 +28,27 @@
  *   qlen   [num_jobs]                 requests per job
  *   klen   [num_jobs]                 positions per job (mutable, see below)
  *   slots  [num_requests, max_slots]  reference slot code job*max_requests+j
- *   counts [num_requests]             partials per request
- * followed by this implementation's own arrays:
- *   slot_base   [num_jobs]                 first compact partial of each job
- *   cslots      [num_requests, max_slots]  compact partial ids per request
- *   small_tasks [num_small_tasks, 2]       (job, 16-row tile) for the SIMT kernel
- *   tc_tasks    [num_tc_tasks, 2]          (job, 128-row tile) for the tcgen05 kernel
+ *   counts [num_requests]             reference partials per request
+ * followed by this implementation's own arrays.  A job is executed as one or
+ * more pieces, contiguous key ranges with their own partial slots:
+ *   pieces      [num_pieces, 4]             job, key offset, keys, first partial slot;
+ *                                           a piece covers keys [offset, offset +
+ *                                           min(keys, klen[job] - offset)) of its job
+ *   pcounts     [num_requests]              partials per request (over pieces)
+ *   cslots      [num_requests, max_pslots]  partial slots of each request
+ *   small_tasks [num_small_tasks, 2]        (piece, 16-row tile), SIMT kernel
+ *   tc_tasks    [num_tc_tasks, 2]           (piece, 256-row pair), query-tile tcgen05 kernel
+ *   kn_offsets  [kn_ctas + 1]               task range of each persistent CTA of the
+ *                                           keys-in-lanes tcgen05 kernel
+ *   kn_tasks    [num_kn_tasks, 4]           its task headers: first segment, segments, 0, 0
+ *   kn_segs     [num_kn_segs, 8]            segments: KV head, first query row in the
+ *                                           task, query rows, first partial slot, first
+ *                                           pool position, first key of its slot in the
+ *                                           tile, keys, job | growing << 30 (growing: keys
+ *                                           = min(keys, klen[job]), a decode tail); a task
+ *                                           of several segments is one 128-key tile
+ * Every array starts at a multiple of 4 int32 (16 bytes).  Partial slot s of a
+ * piece holds query rows s*G .. s*G+G-1 (one request).
  *
  * Return value: 0 on success, otherwise a TA_ERR_* code describing a rejected
  * argument or a launch failure.  Errors found on the device (a metadata index
@@ -49,7 +64,7 @@
 extern "C" {
 #endif
 
-#define TA_ABI_VERSION 2
+#define TA_ABI_VERSION 3
 
 #define TA_DTYPE_BF16 1
 #define TA_DTYPE_F16 2
@@ -70,13 +85,19 @@ typedef struct ta_plan_layout {
   int32_t max_requests;
   int32_t max_slots;
   int32_t num_requests;
-  int32_t num_partials;
+  int32_t num_pieces;
+  int32_t num_partials;  /* partial slots: sum over pieces of their job's requests */
+  int32_t max_pslots;
   int32_t num_small_tasks;
   int32_t num_tc_tasks;
+  int32_t num_kn_tasks;
+  int32_t num_kn_segs;
+  int32_t kn_ctas;       /* persistent CTAs of the keys-in-lanes kernel (<= SM count) */
+  int32_t kn_rows;       /* most query rows of any keys-in-lanes task (<= 64) */
   /* small tasks are sorted by padded row count: [0, e0) need 4 rows,
      [e0, e1) 8 rows, [e1, e2) 16 rows; e2 == num_small_tasks */
   int32_t small_class_end[3];
-  /* longest segment among small tasks when the plan was built (a hint: the
+  /* longest piece among small tasks when the plan was built (a hint: the
      SIMT kernel single-buffers when every task fits one 64-key chunk) */
   int32_t small_max_keys;
   int32_t kstart_stride;
@@ -86,10 +107,14 @@ typedef struct ta_plan_layout {
   int32_t off_klen;
   int32_t off_slots;
   int32_t off_counts;
-  int32_t off_slot_base;
+  int32_t off_pieces;
+  int32_t off_pcounts;
   int32_t off_cslots;
   int32_t off_small_tasks;
   int32_t off_tc_tasks;
+  int32_t off_kn_offsets;
+  int32_t off_kn_tasks;
+  int32_t off_kn_segs;
 } ta_plan_layout;
 
 /* ABI version of the loaded library (TA_ABI_VERSION). */
@@ -99,10 +124,10 @@ int ta_abi_version(void);
 const char* ta_error_string(int code);
 
 /*
- * Partial attention of every (job, KV head) of the plan: for each query row
- * (request of the job x GQA row) the softmax-normalised output over the job's
- * positions and its natural-log LSE, written to part/lse at the row's compact
- * partial slot.  A job with zero positions writes O = 0 and LSE = -inf.
+ * Partial attention of every (piece, KV head) of the plan: for each query row
+ * (request of the piece's job x GQA row) the softmax-normalised output over the
+ * piece's positions and its natural-log LSE, written to part/lse at the row's
+ * partial slot.  A piece with zero positions writes O = 0 and LSE = -inf.
  * Replaces the reference's _segment kernel (kernels.py:8-55) and its two launch
  * phases in attention_matrix (kernels.py:158-165).
  */
@@ -152,6 +177,7 @@ int ta_attention_noalloc(const ta_plan_layout* plan, const int32_t* meta, const 
 /*
  * klen[tail_jobs[i]] = value for i < num_tails, on the device: the per-step
  * update of a reused decode plan, CachedDecodePlan.update (kernels.py:184-186).
+ * A growing tail job must be a single piece (offset 0, keys >= every value).
  */
 int ta_update_tail_klen(int32_t* klen, const int32_t* tail_jobs, int32_t num_tails, int32_t value,
                         int32_t num_jobs, int32_t* status, void* stream);

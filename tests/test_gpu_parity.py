@@ -121,17 +121,18 @@ def test_extreme_logits():
 
 
 def test_segment_partials_match_oracle():
-    """Each (job, request) partial output and LSE, read back from the scratch buffers."""
+    """Each (piece, request) partial output and LSE, read back from the scratch buffers."""
     tree = build_tree(_Lib, SPECS["deep_bench"])
     q, k, v = make_inputs(len(tree.paths), tree.storage_tokens, 32, 8, 128, torch.bfloat16, seed=5)
     plan = schedule(tree, 32, 8, 128, "cube", CostModel(kv_split=200))
     _, _, p = run_kernel(q, k, v, plan)
     part, lse = p.part.cpu(), p.lse.cpu()
-    expected = oracle.job_partials(q.float(), k.float(), v.float(), p.jobs)
-    base = p.host_arrays["slot_base"]
-    for i, (job, (o_ref, l_ref)) in enumerate(zip(p.jobs, expected)):
+    pieces = p.host_arrays["pieces"]
+    piece_jobs = [kernels.Job(p.jobs[j].requests, p.jobs[j].tokens[o:o + n]) for j, o, n, _ in pieces]
+    expected = oracle.job_partials(q.float(), k.float(), v.float(), piece_jobs)
+    for (_, _, _, first), job, (o_ref, l_ref) in zip(pieces, piece_jobs, expected):
         for j in range(len(job.requests)):
-            rows = slice((base[i] + j) * 4, (base[i] + j + 1) * 4)
+            rows = slice((first + j) * 4, (first + j + 1) * 4)
             o = part[:, rows].reshape(32, 128)      # [HK*G, D] == query heads in order
             l = lse[:, rows].reshape(32)
             assert ((o - o_ref[j]).norm(dim=-1) / o_ref[j].norm(dim=-1)).max() <= REL_L2
@@ -252,9 +253,52 @@ def test_tensor_core_pipeline_tile_counts(keys, nreq):
     q, k, v = make_inputs(nreq, keys, 32, 8, 128, torch.bfloat16, seed=keys * 7 + nreq)
     plan = schedule(tree, 32, 8, 128, "fixed", CostModel(kv_split=4096, max_query_rows=4096))
     out, lse, p = run_kernel(q, k, v, plan, pool_pad=200)
-    if nreq * 4 > kernels.SMALL_ROWS:
-        assert p.layout.num_tc_tasks == (nreq * 4 + kernels.TC_ROWS - 1) // kernels.TC_ROWS
+    pieces = p.layout.num_pieces
+    if nreq * 4 > kernels.KN_ROWS:
+        assert p.layout.num_tc_tasks == pieces * ((nreq * 4 + kernels.TC_ROWS - 1) // kernels.TC_ROWS)
+    else:
+        assert p.layout.num_kn_tasks == pieces * 8
     check_against_oracle(q, k, v, tree.paths, out, lse)
+
+
+@pytest.mark.parametrize("keys", [1, 15, 16, 17, 31, 32, 33, 100, 127, 128, 129, 300, 1000])
+@pytest.mark.parametrize("nreq", [1, 3, 4, 5, 8, 9, 16])
+def test_keys_in_lanes_rows_and_tiles(keys, nreq):
+    """Keys-in-lanes tcgen05 kernel: 4..64 query rows (MMA N 16 / 32 / 64), partial
+    32-key boxes, V rows zeroed up to the next 16-key step, NaN in the pool past
+    the segment, multi-tile pieces."""
+    tree = KVTree.synthetic([-1], [keys], [0] * nreq)
+    q, k, v = make_inputs(nreq, keys, 32, 8, 128, torch.bfloat16, seed=keys * 13 + nreq)
+    plan = schedule(tree, 32, 8, 128, "fixed", CostModel(kv_split=4096, max_query_rows=4096))
+    out, lse, p = run_kernel(q, k, v, plan, pool_pad=160)
+    assert p.layout.num_kn_tasks > 0 and p.layout.num_tc_tasks == 0 and p.layout.num_small_tasks == 0
+    assert p.layout.kn_rows >= nreq * 4
+    check_against_oracle(q, k, v, tree.paths, out, lse)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_keys_in_lanes_rising_scores_rescale(dtype):
+    """Scores that keep rising along the segment force the stale-maximum rescale of
+    the sums and of O^T in TMEM on many tiles; plus x30 random logits."""
+    nreq, keys = 6, 1500
+    tree = KVTree.synthetic([-1, 0, 0], [keys, 40, 40], [1, 1, 2, 2, 1, 2])
+    g = torch.Generator().manual_seed(77)
+    q = torch.randn(nreq, 32, 128, generator=g)
+    k = torch.randn(tree.storage_tokens, 8, 128, generator=g) * 0.2
+    v = torch.randn(tree.storage_tokens, 8, 128, generator=g)
+    direction = q.reshape(nreq, 8, 4, 128).mean(dim=(0, 2))          # per KV head
+    ramp = torch.linspace(0, 150.0, tree.storage_tokens)[:, None, None]   # ~40 log2 units of score
+    k = k + ramp * direction[None] / direction.norm(dim=-1, keepdim=True)[None]
+    q, k, v = q.to(dtype), k.to(dtype), v.to(dtype)
+    for method in ("fixed", "cube", "request"):
+        plan = schedule(tree, 32, 8, 128, method, CostModel(kv_split=4096, max_query_rows=4096))
+        out, lse, _ = run_kernel(q, k, v, plan)
+        check_against_oracle(q, k, v, tree.paths, out, lse)
+    q2, k2, v2 = make_inputs(nreq, tree.storage_tokens, 32, 8, 128, dtype, seed=78, scale=30.0)
+    for method in ("fixed", "cube", "request"):
+        plan = schedule(tree, 32, 8, 128, method, CostModel(kv_split=256))
+        out, lse, _ = run_kernel(q2, k2, v2, plan)
+        check_against_oracle(q2, k2, v2, tree.paths, out, lse)
 
 
 def test_evaluation_grid_sample_matches_oracle():

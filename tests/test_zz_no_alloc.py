@@ -50,7 +50,7 @@ def test_noalloc_matches_allocating_entry_point_twice():
         pytest.skip("needs a CUDA device")
     tree, q, kp, vp = _inputs()
     p = prepare(schedule(tree, method="cube", model=CostModel.b200()), q)
-    assert p.layout.num_tc_tasks > 0 and p.layout.num_small_tasks > 0
+    assert p.layout.num_tc_tasks > 0 and p.layout.num_kn_tasks > 0
     ref_out = torch.empty_like(q)
     ref_lse = torch.empty(48, 32, device="cuda")
     assert _call("ta_attention", p, q, kp, vp, ref_out, ref_lse, True) == 0

@@ -14,9 +14,13 @@ namespace {
 
 bool layout_ok(const ta_plan_layout* L) {
   if (!L) return false;
-  if (L->num_jobs < 0 || L->max_requests < 0 || L->max_slots < 0 || L->num_requests < 0 || L->num_partials < 0)
+  if (L->num_jobs < 0 || L->max_requests < 0 || L->max_slots < 0 || L->num_requests < 0 || L->num_pieces < 0 ||
+      L->num_partials < 0 || L->max_pslots < 0)
     return false;
-  if (L->num_small_tasks < 0 || L->num_tc_tasks < 0 || L->kstart_stride < 1) return false;
+  if (L->num_small_tasks < 0 || L->num_tc_tasks < 0 || L->num_kn_tasks < 0 || L->kn_ctas < 0 || L->kstart_stride < 1)
+    return false;
+  if (L->num_kn_tasks > 0 && (L->kn_ctas < 1 || L->kn_rows < 1 || L->kn_rows > 64 || L->num_kn_segs < 1)) return false;
+  if ((L->off_kn_tasks & 3) || (L->off_kn_segs & 3)) return false;   // int4 loads
   const int32_t* e = L->small_class_end;
   if (e[0] < 0 || e[1] < e[0] || e[2] < e[1] || e[2] != L->num_small_tasks) return false;
   return true;
@@ -55,12 +59,14 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
                int32_t head_dim, int32_t dtype, float* part, float* lse, int32_t* status, void* stream) {
   if (!layout_ok(plan) || !meta || pool_tokens < 0) return TA_ERR_ARG;
   if (!heads_ok(num_q_heads, num_kv_heads, head_dim, dtype)) return TA_ERR_UNSUPPORTED;
-  const int tasks = plan->num_small_tasks + plan->num_tc_tasks;
+  const int tasks = plan->num_small_tasks + plan->num_tc_tasks + plan->num_kn_tasks;
   if (tasks == 0) return TA_OK;
   if (!q || !kpool || !vpool || !part || !lse) return TA_ERR_ARG;
   // bulk copies and TMA need 16-byte aligned bases; rows are 2*head_dim bytes
   if (!aligned16(q) || !aligned16(kpool) || !aligned16(vpool) || !aligned16(part)) return TA_ERR_ARG;
-  if (plan->num_tc_tasks > 0 && head_dim != 128) return TA_ERR_UNSUPPORTED;
+  if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && head_dim != 128) return TA_ERR_UNSUPPORTED;
+  // TMA coordinates are 32-bit
+  if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && pool_tokens > int64_t(INT32_MAX) - 512) return TA_ERR_ARG;
 
   SegParams p{};
   p.q = static_cast<const uint16_t*>(q);
@@ -72,12 +78,16 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
   p.kstart = meta + plan->off_kstart;
   p.qlen = meta + plan->off_qlen;
   p.klen = meta + plan->off_klen;
-  p.slot_base = meta + plan->off_slot_base;
+  p.pieces = meta + plan->off_pieces;
   p.small_tasks = meta + plan->off_small_tasks;
   p.tc_tasks = meta + plan->off_tc_tasks;
+  p.kn_offsets = meta + plan->off_kn_offsets;
+  p.kn_tasks = meta + plan->off_kn_tasks;
+  p.kn_segs = meta + plan->off_kn_segs;
   p.status = status;
   p.pool_tokens = pool_tokens;
   p.num_jobs = plan->num_jobs;
+  p.num_pieces = plan->num_pieces;
   p.max_requests = plan->max_requests;
   p.kstart_stride = plan->kstart_stride;
   p.num_requests = plan->num_requests;
@@ -85,11 +95,15 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
   p.num_q_heads = num_q_heads;
   p.num_kv_heads = num_kv_heads;
   p.group = num_q_heads / num_kv_heads;
+  p.num_kn_tasks = plan->num_kn_tasks;
+  p.num_kn_segs = plan->num_kn_segs;
+  p.kn_ctas = plan->kn_ctas;
   p.scale_log2 = kLog2e / std::sqrt(float(head_dim));
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err = cudaSuccess;
   if (plan->num_tc_tasks > 0) err = launch_seg_tc(p, plan->num_tc_tasks, dtype, s);
+  if (err == cudaSuccess && plan->num_kn_tasks > 0) err = launch_seg_kn(p, plan->kn_rows, dtype, s);
   if (err == cudaSuccess && plan->num_small_tasks > 0)
     err = launch_seg_simt(p, plan->small_class_end, plan->small_max_keys, head_dim, dtype, s);
   return launch_status(err);
@@ -106,12 +120,12 @@ int ta_merge(const ta_plan_layout* plan, const int32_t* meta, const float* part,
   p.part = part;
   p.lse = lse;
   p.cslots = meta + plan->off_cslots;
-  p.counts = meta + plan->off_counts;
+  p.counts = meta + plan->off_pcounts;
   p.out = out;
   p.out_lse = out_lse;
   p.status = status;
   p.num_requests = plan->num_requests;
-  p.max_slots = plan->max_slots;
+  p.max_slots = plan->max_pslots;
   p.num_partials = plan->num_partials;
   p.num_q_heads = num_q_heads;
   p.group = num_q_heads / num_kv_heads;

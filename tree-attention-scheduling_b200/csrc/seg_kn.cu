@@ -1,0 +1,836 @@
+// Segment attention for small query groups (<= 64 rows per piece x KV head) on
+// the 5th-generation tensor cores, with the keys in the TMEM lanes.
+//
+// A decode-time job shared by a few requests has few query rows (requests x
+// GQA group, e.g. 4 for a private leaf) and many keys.  Putting the keys on the
+// MMA's M side and the queries on N makes such a job a thin tcgen05 problem:
+//   S^T [128 keys x N] = K_tile [128 x 128 dims] . Q^T          (kind::f16, both K-major)
+//   O^T [128 dims x N] += V_tile^T [128 dims x 128 keys] . P^T  (A = V MN-major, B = P K-major)
+// with N = max(16, R) for a row class R in {4, 8, 16, 32, 64}; only R rows are
+// touched on the CUDA cores.  Each thread of the softmax warps owns one key of
+// the tile (one TMEM lane), so scores need no cross-lane reduction; row sums
+// are kept per thread and reduced once per task.  Row maxima are handled with
+// a stale maximum: the softmax uses the last agreed maximum m_r and only when
+// some live key of the tile exceeds m_r + 8 (log2 units) do the warps agree
+// (bar.red.or) on a new maximum and rescale their sums and the O^T columns in
+// TMEM.  Every result is exact after the final division; P <= 2^8 keeps the
+// bf16 P and f32 sums safe.
+//
+// Tasks.  A task is either one long segment (a piece of a job for one KV head)
+// spanning several 128-key tiles, or up to four short segments packed into ONE
+// tile: each segment owns a slot of the tile's keys (32-key aligned, slots
+// back to back) and a range of the N query rows, and a row only sees the keys
+// of its own segment.  Packing turns the many one-tile private leaves of a
+// decode tree into full tiles, so their fixed per-tile costs are shared.
+//
+// The kernel is persistent: one CTA per SM walks a host-built list of tasks
+// (longest-processing-time balanced).  A scheduler warp decodes and checks
+// each task ONCE into a ring of shared-memory task slots and gathers its Q^T
+// rows, running ahead of every other role; the K and V TMA producers run ahead
+// across task boundaries too, so the HBM stream does not stop between short
+// tasks and no role waits on global-memory metadata.  Loads are 32-key boxes
+// (64 columns, 128-byte swizzle, no multicast).  P.V reads V rows up to the
+// next 16-key step past the last live key; any of those rows that is not a
+// live key of its slot (rows a box brought in past its segment, the rest of an
+// empty or short slot) is zeroed first -- pool rows there may hold anything.
+//
+//   warps 0-3  softmax (thread = key = TMEM lane) and the per-task epilogue
+//              (thread = head dim = TMEM lane of O^T), deferred until after
+//              the next task's first tile so its P.V has time to finish
+//   warp 4     K producer (ring of STAGES 32 KB tiles)
+//   warp 5     V producer
+//   warp 6     MMA issue (lane 0): waits, zeroes V rows where needed, issues
+//              P.V(g), then S(g+2)
+//   warp 7     scheduler: task slots (decode + checks) and Q^T gathers into
+//              two buffers, each released by the MMA's commit after the last S
+//              of its previous task
+//
+// Ordering facts the barrier scheme relies on: MMAs issued by one thread run in
+// issue order, and the issue order is S(0) S(1) PV(0) S(2) PV(1) S(3) ..., so
+// observing S(g) complete implies PV(g-2) has completed.  A parity wait is only
+// correct while its barrier is at most one phase behind, so every per-tile
+// barrier exists twice, by tile parity (S_FULL, P_FULL, PV_DONE): waiting for
+// PV(g) or PV(g-1) after observing S(g) then never aliases.  All waits are
+// bounded and every decision that guards a named barrier is made CTA-uniform
+// first.
+//
+// TMEM columns: [0, N) and [N, 2N) S^T (by tile parity), [2N, 3N) and
+// [3N, 4N) O^T (by task parity: a task's epilogue runs after the next task's
+// first tile, while that task already accumulates into the other buffer).
+// The reference's _segment (kernels.py:8-55) computes the same partial O / LSE
+// per (job, KV head) with Triton tiles of 16 query rows x 64 keys.
+#include "ta_kernels.cuh"
+#include "tc_common.cuh"
+
+namespace ta {
+
+namespace {
+
+constexpr int kKeys = 128;                  // keys per tile = MMA M = TMEM lanes
+constexpr int kDim = 128;                   // head_dim
+constexpr int kBoxRows = 32;                // TMA box height
+constexpr int kSegMax = 4;                  // segments packed into one tile
+constexpr int kTQ = 8;                      // task slots
+constexpr int kSoftmaxThreads = 128;
+constexpr int kKWarp = 4, kVWarp = 5, kMmaWarp = 6, kSchedWarp = 7;
+constexpr int kThreads = 8 * 32;
+constexpr uint32_t kTileBytes = kKeys * kDim * 2;          // 32 KB
+constexpr uint32_t kHalfBytes = kTileBytes / 2;            // one 64-column swizzled block
+constexpr uint32_t kBoxBytes = kBoxRows * 128;              // one 32-row x 64-column box
+constexpr float kRescaleThreshold = 8.0f;                   // log2 units
+// task slot words: nseg, ntiles, rows, flags, then per segment
+// head, row0, rows, keys now, first key of its slot, slot keys, job, k0, first partial row
+constexpr int kSegWords = 9;
+constexpr int kTaskWords = 4 + kSegMax * kSegWords;         // 40
+enum TaskFlag { TASK_BAD = 1, TASK_WRITE = 2 };
+enum SegField { F_HEAD, F_ROW0, F_ROWS, F_NK, F_KT, F_SPAN, F_JOB, F_K0, F_PROW0 };
+
+template <int R>
+struct KnCfg {
+  static constexpr int N = R < 16 ? 16 : R;                 // MMA N
+  static constexpr int CW = R < 16 ? R : 16;                // TMEM columns per load
+  static constexpr int NC = R / CW;                          // loads per row set
+  static constexpr int kStages = N <= 16 ? 3 : 2;
+  static constexpr uint32_t kQHalf = N * 128;               // 64-column block of N rows
+  static constexpr uint32_t kQBytes = 2 * kQHalf;           // Q^T or P^T buffer
+  static constexpr uint32_t off_k = 0;
+  static constexpr uint32_t off_v = off_k + kStages * kTileBytes;
+  static constexpr uint32_t off_q = off_v + kStages * kTileBytes;    // Q^T[2]
+  static constexpr uint32_t off_p = off_q + 2 * kQBytes;              // P^T[2]
+  static constexpr uint32_t off_red = off_p + 2 * kQBytes;            // [2][4][R] tile maxima by tile parity
+  static constexpr uint32_t off_suml = off_red + 2 * 4 * R * 4;       // [2][4][R] row sums per warp, by task parity
+  static constexpr uint32_t off_mfin = off_suml + 2 * 4 * R * 4;      // [2][R] final row maxima, by task parity
+  static constexpr uint32_t off_tasks = off_mfin + 2 * R * 4;         // [kTQ][kTaskWords] task slots
+  static constexpr uint32_t off_bar = off_tasks + kTQ * kTaskWords * 4;
+  // k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], q_full[2], pv_done[2],
+  // q_empty[2], task_full[kTQ], task_empty[kTQ]
+  static constexpr int kBars = 4 * kStages + 10 + 2 * kTQ;
+  static constexpr uint32_t off_tmem = off_bar + kBars * 8;
+  static constexpr uint32_t bytes = off_tmem + 16;
+  static constexpr uint32_t alloc = bytes + 1024;             // slack to align the base to 1 KB
+  static constexpr uint32_t kTmemCols = N == 16 ? 64 : (N == 32 ? 128 : 256);
+  static_assert(alloc <= 227 * 1024, "shared memory budget");
+  static_assert(4 * N <= kTmemCols, "TMEM budget");
+};
+
+// Header of list entry i: first segment, segment count, 0, 0.
+__device__ __forceinline__ int4 load_header(const SegParams& p, int i) {
+  return reinterpret_cast<const int4*>(p.kn_tasks)[i];
+}
+
+// Decode and check list entry `i` into a task slot (one thread).  Segments as
+// the host wrote them (8 int32): KV head, first query row of the tile's N
+// rows, rows, first partial slot, first pool position, first key of its slot
+// in the tile, keys (at most), job | growing << 30.
+template <int R>
+__device__ __noinline__ void decode_task(const SegParams& p, int i, int* w) {
+  w[0] = w[1] = w[2] = 0;
+  w[3] = TASK_BAD;
+  const int4 h = load_header(p, i);
+  const int first = h.x, nseg = h.y;
+  if (nseg < 1 || nseg > kSegMax || first < 0 || int64_t(first) + nseg > p.num_kn_segs) return;
+  const int G = p.group;
+  const int4* segs = reinterpret_cast<const int4*>(p.kn_segs) + 2 * int64_t(first);
+  int rows = 0, slot_end = 0, bad = 0, any = 0;
+  for (int s = 0; s < nseg; ++s) {
+    const int4 a = segs[2 * s], b = segs[2 * s + 1];
+    int* sw = w + 4 + s * kSegWords;
+    const int head = a.x, row0 = a.y, srows = a.z, slot = a.w, k0 = b.x, kt = b.y, kmax = b.z;
+    const int job = b.w & 0x3fffffff, growing = (b.w >> 30) & 1;
+    const int span = ((kmax + kBoxRows - 1) / kBoxRows) * kBoxRows;
+    if (head < 0 || head >= p.num_kv_heads || job < 0 || job >= p.num_jobs || srows < 1 || srows % G ||
+        srows / G > p.max_requests || row0 != rows || slot < 0 || int64_t(slot) + srows / G > p.num_partials ||
+        kmax < 0 || kt != slot_end || (nseg > 1 && kt + span > kKeys) ||
+        int64_t(p.num_partials) * G > INT32_MAX)
+      return;                                      // nothing of this task may be written
+    int nk = kmax;
+    if (growing) nk = min(kmax, p.klen[job]);      // a growing decode tail (always a whole job)
+    if (nk < 0) nk = 0;
+    if (k0 < 0 || int64_t(k0) + nk > p.pool_tokens || k0 > INT32_MAX - 512) {
+      nk = 0;
+      bad = 1;
+    }
+    sw[F_HEAD] = head;
+    sw[F_ROW0] = row0;
+    sw[F_ROWS] = srows;
+    sw[F_NK] = nk;
+    sw[F_KT] = kt;
+    sw[F_SPAN] = nseg == 1 ? kKeys : span;
+    sw[F_JOB] = job;
+    sw[F_K0] = k0;
+    sw[F_PROW0] = slot * G;
+    rows += srows;
+    slot_end = kt + span;
+    any |= nk;
+  }
+  if (rows > R) return;
+  w[0] = nseg;
+  w[1] = nseg == 1 ? (w[4 + F_NK] + kKeys - 1) / kKeys : (any ? 1 : 0);
+  w[2] = rows;
+  w[3] = TASK_WRITE | (bad ? TASK_BAD : 0);
+}
+
+// Keys of segment s of a task slot inside tile j (a packed task has one tile).
+__device__ __forceinline__ int slot_keys(const int* w, int s, int j) {
+  const int nk = w[4 + s * kSegWords + F_NK];
+  return w[0] == 1 ? min(kKeys, nk - j * kKeys) : nk;
+}
+
+__device__ __forceinline__ uint64_t row_mask(int row0, int rows) {
+  return (rows >= 64 ? ~0ull : ((1ull << rows) - 1ull)) << row0;
+}
+
+// Byte offset of element (row r, column c) of a K-major operand held as two
+// 64-column blocks of `half` bytes with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t swz(uint32_t half, int r, int c) {
+  return uint32_t(c >> 6) * half + uint32_t(r) * 128u + ((uint32_t((c & 63) >> 3) ^ uint32_t(r & 7)) << 4) +
+         uint32_t(c & 7) * 2u;
+}
+
+// Float max over the warp as an order-preserving unsigned key (redux.sync).
+__device__ __forceinline__ float warp_max_redux(float x) {
+  const uint32_t b = __float_as_uint(x);
+  const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  uint32_t r;
+  asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(k));
+  return __uint_as_float((r & 0x80000000u) ? (r & 0x7fffffffu) : ~r);
+}
+
+// W consecutive 32-bit TMEM columns of this thread's lane (W = 4, 8 or 16).
+template <int W>
+__device__ __forceinline__ void tmem_ldw(uint32_t taddr, uint32_t (&r)[W]) {
+  if constexpr (W == 16) {
+    tmem_ld16(taddr, r);
+  } else if constexpr (W == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+  } else {
+    static_assert(W == 4, "column group");
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+  }
+}
+template <int W>
+__device__ __forceinline__ void tmem_stw(uint32_t taddr, const uint32_t (&r)[W]) {
+  if constexpr (W == 16) {
+    tmem_st16(taddr, r);
+  } else if constexpr (W == 8) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]));
+  } else {
+    static_assert(W == 4, "column group");
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3]));
+  }
+}
+
+template <typename T, int R>
+__global__ void __launch_bounds__(kThreads, 1)
+    seg_kn_kernel(SegParams p, const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v) {
+  using C = KnCfg<R>;
+  constexpr int N = C::N, CW = C::CW, NC = C::NC;
+  constexpr int S = C::kStages;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::off_bar);
+  uint64_t* k_full = bars;
+  uint64_t* k_empty = bars + S;
+  uint64_t* v_full = bars + 2 * S;
+  uint64_t* v_empty = bars + 3 * S;
+  uint64_t* s_full = bars + 4 * S;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* q_full = s_full + 4;
+  uint64_t* pv_done = s_full + 6;   // [2], by tile parity
+  uint64_t* q_empty = s_full + 8;   // [2], by Q^T buffer
+  uint64_t* task_full = s_full + 10;
+  uint64_t* task_empty = task_full + kTQ;
+  int* tasks = reinterpret_cast<int*>(smem + C::off_tasks);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::off_tmem);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = p.group;
+  int begin = p.kn_offsets[blockIdx.x], end = p.kn_offsets[blockIdx.x + 1];
+  if (begin < 0 || end < begin || end > p.num_kn_tasks) {
+    if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
+    begin = end = 0;
+  }
+  const int count = end - begin;
+  auto slot_of = [&](int k) { return tasks + (k % kTQ) * kTaskWords; };   // k: index within this CTA's list
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&q_full[b], 1);
+      mbar_init(&pv_done[b], 1);
+      mbar_init(&q_empty[b], 1);
+    }
+    for (int b = 0; b < kTQ; ++b) {
+      mbar_init(&task_full[b], 1);
+      mbar_init(&task_empty[b], 7);   // K, V, MMA and the 4 softmax warps
+    }
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kSchedWarp) {
+    // ---------------- scheduler: task slots and Q^T gathers ----------------
+    unsigned char* qbuf = smem + C::off_q;
+    int qi = 0;
+    bool alive = true;
+    for (int k = 0; k < count && alive; ++k) {
+      int* w = slot_of(k);
+      if (k >= kTQ) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(&task_empty[k % kTQ], ((k / kTQ) - 1) & 1, p.status);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) { alive = false; break; }
+      }
+      if (lane == 0) {
+        decode_task<R>(p, begin + k, w);
+        mbar_arrive(&task_full[k % kTQ]);
+      }
+      __syncwarp();
+      if (w[0] == 0 || w[1] == 0) continue;          // no tiles: no Q^T
+      const int qb = qi & 1;
+      if (qi >= 2) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(&q_empty[qb], ((qi >> 1) - 1) & 1, p.status);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) { alive = false; break; }
+      }
+      // rows x 16 chunks of 16 bytes, swizzled K-major
+      unsigned char* dst = qbuf + qb * C::kQBytes;
+      const int rows = w[2];
+      for (int e = lane; e < rows * 16; e += 32) {
+        const int r = e >> 4, c = e & 15;
+        int s = 0;
+#pragma unroll
+        for (int x = 1; x < kSegMax; ++x)
+          if (x < w[0] && r >= w[4 + x * kSegWords + F_ROW0]) s = x;
+        const int* sw = w + 4 + s * kSegWords;
+        const int lr = r - sw[F_ROW0];
+        const int rid = p.qids[int64_t(sw[F_JOB]) * p.max_requests + lr / G];
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (rid >= 0 && rid < p.num_requests)
+          v = *reinterpret_cast<const uint4*>(p.q + (int64_t(rid) * p.num_q_heads + sw[F_HEAD] * G + lr % G) * kDim + c * 8);
+        else
+          set_status(p.status, TA_ERR_BOUNDS);
+        *reinterpret_cast<uint4*>(dst + (c >> 3) * C::kQHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_full[qb]);
+      ++qi;
+    }
+  } else if (warp == kKWarp || warp == kVWarp) {
+    // ---------------- TMA producers ----------------
+    if (lane == 0) {
+      const bool is_k = warp == kKWarp;
+      const CUtensorMap* map = is_k ? &tmap_k : &tmap_v;
+      unsigned char* ring = smem + (is_k ? C::off_k : C::off_v);
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      int g = 0;
+      bool alive = true;
+      for (int k = 0; k < count && alive; ++k) {
+        if (!mbar_wait(&task_full[k % kTQ], (k / kTQ) & 1, p.status)) break;
+        const int* w = slot_of(k);
+        const int nseg = w[0], ntiles = w[1];
+        for (int j = 0; j < ntiles; ++j, ++g) {
+          const int st = g % S;
+          if (g >= S && !mbar_wait(&empty[st], ((g / S) + 1) & 1, p.status)) { alive = false; break; }
+          int boxes_total = 0;
+#pragma unroll 1
+          for (int s = 0; s < nseg; ++s) boxes_total += (max(0, slot_keys(w, s, j)) + kBoxRows - 1) / kBoxRows;
+          mbar_arrive_expect_tx(&full[st], uint32_t(boxes_total) * 2 * kBoxBytes);
+          unsigned char* dst = ring + st * kTileBytes;
+          // (loops kept rolled: unrolled copies of the TMA issue made the
+          // kernel outgrow the instruction cache)
+#pragma unroll 1
+          for (int s = 0; s < nseg; ++s) {
+            const int* sw = w + 4 + s * kSegWords;
+            const int keys = max(0, slot_keys(w, s, j));
+            const int y = sw[F_K0] + j * kKeys;
+#pragma unroll 1
+            for (int b = 0; b * kBoxRows < keys; ++b) {
+              const uint32_t row = uint32_t(sw[F_KT] + b * kBoxRows) * 128u;
+              tma_load_3d(dst + row, map, 0, y + b * kBoxRows, sw[F_HEAD], &full[st]);
+              tma_load_3d(dst + kHalfBytes + row, map, 64, y + b * kBoxRows, sw[F_HEAD], &full[st]);
+            }
+          }
+        }
+        mbar_arrive(&task_empty[k % kTQ]);
+      }
+      // Nothing may still be landing when the CTA exits: wait (bounded) for
+      // the last loads of each ring slot.
+      for (int q = max(0, g - S); q < g; ++q)
+        if (!mbar_wait(&full[q % S], (q / S) & 1, p.status)) break;
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issue (lane 0) ----------------
+    if (lane == 0) {
+      constexpr uint32_t ab = Elem<T>::kCode == TA_DTYPE_BF16 ? 1u : 0u;
+      constexpr uint32_t idesc_s = umma_idesc(ab, 0, 0, kKeys, N);    // A = K tile, B = Q^T
+      constexpr uint32_t idesc_pv = umma_idesc(ab, 1, 0, kDim, N);    // A = V^T (MN-major), B = P^T
+      const uint64_t kdesc0 = smem_desc(smem_u32(smem + C::off_k), 16, 1024);
+      const uint64_t vdesc0 = smem_desc(smem_u32(smem + C::off_v), kHalfBytes, 1024);
+      const uint64_t qdesc0 = smem_desc(smem_u32(smem + C::off_q), 16, 1024);
+      const uint64_t pdesc0 = smem_desc(smem_u32(smem + C::off_p), 16, 1024);
+      bool alive = true;
+
+      // Two cursors over the CTA's tiles: `sc` issues S two tiles ahead of `pc`.
+      // Tasks without tiles are skipped; `qi` counts the tasks with tiles,
+      // which alone use the Q^T and O^T buffers.  The S cursor waits for each
+      // task slot; the P.V cursor, which trails it, releases every slot.
+      struct Cursor {
+        int k, j, g, qi;      // index within the list, tile in task, global tile, index among tasks with tiles
+        const int* w;
+      };
+      auto settle = [&](Cursor& c, bool lead) {   // move to the next task with tiles
+        while (c.k < count) {
+          if (lead && !mbar_wait(&task_full[c.k % kTQ], (c.k / kTQ) & 1, p.status)) {
+            alive = false;
+            c.k = count;
+            return;
+          }
+          c.w = slot_of(c.k);
+          if (c.w[0] > 0 && c.w[1] > 0) return;
+          if (!lead) mbar_arrive(&task_empty[c.k % kTQ]);
+          ++c.k;
+        }
+      };
+      auto advance = [&](Cursor& c, bool lead) {
+        ++c.g;
+        if (++c.j >= c.w[1]) {
+          if (!lead) mbar_arrive(&task_empty[c.k % kTQ]);
+          c.j = 0;
+          ++c.k;
+          ++c.qi;
+          settle(c, lead);
+        }
+      };
+      auto issue_s = [&](const Cursor& c) -> bool {
+        const int st = c.g % S;
+        if (c.j == 0 && !mbar_wait(&q_full[c.qi & 1], (c.qi >> 1) & 1, p.status)) return false;
+        if (!mbar_wait(&k_full[st], (c.g / S) & 1, p.status)) return false;
+        tc_fence_after();
+        const uint64_t kd = kdesc0 + ((uint64_t(st) * kTileBytes) >> 4);
+        const uint64_t qd = qdesc0 + ((uint64_t(c.qi & 1) * C::kQBytes) >> 4);
+        const uint32_t d = tmem + uint32_t(c.g & 1) * N;
+#pragma unroll
+        for (int s = 0; s < kDim / 16; ++s) {
+          const uint64_t ka = ((s >> 2) * kHalfBytes + (s & 3) * 32) >> 4;
+          const uint64_t qa = ((s >> 2) * C::kQHalf + (s & 3) * 32) >> 4;
+          umma_ss(d, kd + ka, qd + qa, idesc_s, s > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[c.g & 1]);
+        umma_commit(&k_empty[st]);
+        if (c.j == c.w[1] - 1) umma_commit(&q_empty[c.qi & 1]);    // the task's last S: its Q^T buffer is free
+        return true;
+      };
+      // P.V reads key rows [0, 16 * steps); every such row that is not a live
+      // key of its slot is zeroed first.
+      auto issue_pv = [&](const Cursor& c) -> bool {
+        const int st = c.g % S;
+        if (!mbar_wait(&p_full[c.g & 1], (c.g >> 1) & 1, p.status)) return false;
+        if (!mbar_wait(&v_full[st], (c.g / S) & 1, p.status)) return false;
+        const int* w = c.w;
+        const int nseg = w[0];
+        int steps = 8;
+        if (nseg > 1 || slot_keys(w, 0, c.j) < kKeys) {
+          unsigned char* vt = smem + C::off_v + st * kTileBytes;
+          int extent = 0;
+#pragma unroll 1
+          for (int s = 0; s < nseg; ++s)
+            if (slot_keys(w, s, c.j) > 0) extent = w[4 + s * kSegWords + F_KT] + slot_keys(w, s, c.j);
+          steps = (extent + 15) >> 4;
+          bool zeroed = false;
+#pragma unroll 1
+          for (int s = 0; s < nseg; ++s) {
+            const int kt = w[4 + s * kSegWords + F_KT];
+            const int lo = kt + max(0, slot_keys(w, s, c.j));
+            const int hi = min(kt + w[4 + s * kSegWords + F_SPAN], 16 * steps);
+#pragma unroll 1
+            for (int r = lo; r < hi; ++r) {
+#pragma unroll
+              for (int c16 = 0; c16 < 16; ++c16)
+                *reinterpret_cast<uint4*>(vt + (c16 >> 3) * kHalfBytes + r * 128 + (c16 & 7) * 16) = make_uint4(0, 0, 0, 0);
+            }
+            zeroed |= hi > lo;
+          }
+          if (zeroed) fence_async_smem();
+        }
+        tc_fence_after();
+        const uint64_t vd = vdesc0 + ((uint64_t(st) * kTileBytes) >> 4);
+        const uint64_t pd = pdesc0 + ((uint64_t(c.g & 1) * C::kQBytes) >> 4);
+        const uint32_t o = tmem + 2 * N + uint32_t(c.qi & 1) * N;     // O^T of this task's parity
+#pragma unroll 1
+        for (int s = 0; s < steps; ++s) {
+          const uint64_t va = (uint64_t(s) * 2048) >> 4;           // 16 keys = two 8-row atoms
+          const uint64_t pa = ((s >> 2) * C::kQHalf + (s & 3) * 32) >> 4;
+          umma_ss(o, vd + va, pd + pa, idesc_pv, (c.j > 0 || s > 0) ? 1u : 0u);
+        }
+        umma_commit(&v_empty[st]);
+        umma_commit(&pv_done[c.g & 1]);
+        return true;
+      };
+
+      Cursor sc{0, 0, 0, 0, nullptr}, pc{0, 0, 0, 0, nullptr};
+      settle(sc, true);
+      for (int k = 0; k < 2 && sc.k < count && alive; ++k) {
+        alive = issue_s(sc);
+        advance(sc, true);
+      }
+      if (alive) settle(pc, false);
+      // P.V(g) as soon as its inputs are in, then S(g+2).  P.V(g) must not wait
+      // for S(g+2)'s inputs: those depend on softmax progress that waits for P.V(g).
+      while (pc.k < count && alive) {
+        alive = issue_pv(pc);
+        if (!alive) break;
+        advance(pc, false);
+        if (sc.k < count) {
+          alive = issue_s(sc);
+          advance(sc, true);
+        }
+      }
+      // The last commits must land before the CTA's shared memory is released.
+      const int total = pc.g;
+      if (alive) {
+        for (int q = max(0, total - S); q < total; ++q) {
+          if (!mbar_wait(&k_empty[q % S], (q / S) & 1, p.status)) break;
+          if (!mbar_wait(&v_empty[q % S], (q / S) & 1, p.status)) break;
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax / epilogue (warps 0-3) ----------------
+    const int kk = tid;                                   // key of the tile = TMEM lane; head dim in the epilogue
+    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+    float* red = reinterpret_cast<float*>(smem + C::off_red);      // [2][4][R]
+    float* suml = reinterpret_cast<float*>(smem + C::off_suml);    // [2][4][R] by task parity
+    float* mfin = reinterpret_cast<float*>(smem + C::off_mfin);    // [2][R] by task parity
+    unsigned char* pbuf = smem + C::off_p;
+    const float scale = p.scale_log2;
+    const int64_t head_stride = int64_t(p.num_partials) * G;
+    bool alive = true;
+
+    // Partial row of task row r (rows are laid out segment after segment).
+    auto out_row = [&](const int* w, int r) -> int64_t {
+      int s = 0;
+#pragma unroll
+      for (int x = 1; x < kSegMax; ++x)
+        if (x < w[0] && r >= w[4 + x * kSegWords + F_ROW0]) s = x;
+      const int* sw = w + 4 + s * kSegWords;
+      return int64_t(sw[F_HEAD]) * head_stride + sw[F_PROW0] + (r - sw[F_ROW0]);
+    };
+    auto release = [&](int k) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&task_empty[k % kTQ]);
+    };
+    // Epilogue of a task with tiles whose last tile was `g_last` and whose O^T
+    // and row statistics sit in buffer `b`: O / l and the LSE of every row.
+    auto epilogue = [&](int k, int g_last, int b) {
+      const int* w = slot_of(k);
+      const bool w_ok = alive && warp_wait(&pv_done[g_last & 1], (g_last >> 1) & 1, p.status);
+      if (named_sync_or(2, kSoftmaxThreads, !w_ok)) alive = false;     // also orders suml / mfin
+      const bool o_ok = alive;
+      if (o_ok) tc_fence_after();
+      const float* sl = suml + b * 4 * R;
+      const float* mf = mfin + b * R;
+      const int rows = w[2];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        if (c * CW < rows) {
+          float z[CW], mr[CW];
+#pragma unroll
+          for (int q = 0; q < CW; ++q) {         // all loads before the global stores below
+            const int r = c * CW + q;
+            z[q] = (sl[r] + sl[R + r]) + (sl[2 * R + r] + sl[3 * R + r]);
+            mr[q] = mf[r];
+          }
+          uint32_t o[CW];
+          if (o_ok) {
+            tmem_ldw<CW>(lane_base + 2 * N + uint32_t(b) * N + c * CW, o);
+            tmem_wait_ld();
+          }
+#pragma unroll
+          for (int q = 0; q < CW; ++q) {
+            const int r = c * CW + q;
+            if (r < rows) {
+              const int64_t row = out_row(w, r);
+              const bool live = o_ok && z[q] > 0.f;
+              p.part[row * kDim + kk] = live ? __uint_as_float(o[q]) * (1.f / z[q]) : 0.f;
+              if (kk == r) p.lse[row] = live ? (mr[q] + fast_log2(z[q])) * kLn2 : -INFINITY;
+            }
+          }
+        }
+      }
+      release(k);
+    };
+
+    int g = 0;            // global tile index
+    int qi = 0;           // index among tasks with tiles
+    int pend_k = -1, pend_g = 0;   // task whose epilogue is deferred past the next task's first tile
+    float m[R];           // agreed row maxima of the current task (identical in every thread)
+    for (int k = 0; k < count; ++k) {
+      const bool t_ok = alive && warp_wait(&task_full[k % kTQ], (k / kTQ) & 1, p.status);
+      if (named_sync_or(1, kSoftmaxThreads, !t_ok)) alive = false;
+      if (!alive) break;
+      const int* w = slot_of(k);
+      const int nseg = w[0], ntiles = w[1], rows = w[2], flags = w[3];
+      if ((flags & TASK_BAD) && kk == 0) set_status(p.status, TA_ERR_BOUNDS);
+      if (!(flags & TASK_WRITE)) {
+        release(k);
+        continue;
+      }
+      if (ntiles == 0) {
+        // an empty task: O = 0, LSE = -inf, no tensor work
+        for (int r = 0; r < rows; ++r) {
+          const int64_t row = out_row(w, r);
+          p.part[row * kDim + kk] = 0.f;
+          if (kk == r) p.lse[row] = -INFINITY;
+        }
+        release(k);
+        continue;
+      }
+      float l[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        l[r] = 0.f;
+        m[r] = -INFINITY;
+      }
+
+      for (int j = 0; j < ntiles; ++j, ++g) {
+        const int b = g & 1;
+        // rows whose segment has this thread's key as a live key in this tile
+        uint64_t live_rows = 0;
+#pragma unroll 1
+        for (int s = 0; s < nseg; ++s) {
+          const int* sw = w + 4 + s * kSegWords;
+          const int lo = sw[F_KT], keys = slot_keys(w, s, j);
+          if (kk >= lo && kk < lo + keys) live_rows |= row_mask(sw[F_ROW0], sw[F_ROWS]);
+        }
+        const bool ok = alive && warp_wait(&s_full[b], (g >> 1) & 1, p.status);
+        const uint32_t s_addr = lane_base + uint32_t(b) * N;
+        uint32_t keep[CW];          // scores of the first (for R <= 16: the only) column group
+        bool need = false;
+        if (ok) {
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            if (c * CW < rows) {
+              uint32_t raw[CW];
+              tmem_ldw<CW>(s_addr + c * CW, raw);
+              tmem_wait_ld();
+#pragma unroll
+              for (int q = 0; q < CW; ++q) {
+                const int r = c * CW + q;
+                need |= ((live_rows >> r) & 1ull) && __uint_as_float(raw[q]) * scale > m[r] + kRescaleThreshold;
+                if (c == 0) keep[q] = raw[q];
+              }
+            }
+          }
+        }
+        // One barrier in the common case: the OR of "a wait was lost" and "a
+        // row needs a new maximum"; a second one tells the two apart.
+        bool rescale = false;
+        if (named_sync_or(1, kSoftmaxThreads, need || !ok)) {
+          if (named_sync_or(1, kSoftmaxThreads, !ok))
+            alive = false;
+          else
+            rescale = true;
+        }
+        if (rescale) {
+          // tile maxima over each row's live keys: warp maxima, then the 4 warps
+          float* rt = red + b * 4 * R;
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            if (c * CW < rows) {
+              uint32_t raw[CW];
+              if (c == 0) {
+#pragma unroll
+                for (int q = 0; q < CW; ++q) raw[q] = keep[q];
+              } else {
+                tmem_ldw<CW>(s_addr + c * CW, raw);
+                tmem_wait_ld();
+              }
+              float wm[CW];
+#pragma unroll
+              for (int q = 0; q < CW; ++q) {
+                const int r = c * CW + q;
+                wm[q] = (r < rows) ? warp_max_redux(((live_rows >> r) & 1ull) ? __uint_as_float(raw[q]) * scale
+                                                                                : -INFINITY)
+                                   : -INFINITY;
+              }
+              if (lane == 0) {
+#pragma unroll
+                for (int q = 0; q < CW; q += 4)
+                  *reinterpret_cast<float4*>(rt + warp * R + c * CW + q) = make_float4(wm[q], wm[q + 1], wm[q + 2], wm[q + 3]);
+              }
+            }
+          }
+          named_sync(2, kSoftmaxThreads);
+          bool o_ok = j > 0;
+          if (j > 0) {
+            const bool w_ok = warp_wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, p.status);
+            if (named_sync_or(2, kSoftmaxThreads, !w_ok)) alive = false;
+            o_ok = alive;
+            if (o_ok) tc_fence_after();
+          }
+          const uint32_t o_addr = lane_base + 2 * N + uint32_t(qi & 1) * N;
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            if (c * CW < rows) {
+              float alpha[CW];
+#pragma unroll
+              for (int q = 0; q < CW; ++q) {       // no stores in this loop: the loads batch
+                const int r = c * CW + q;
+                const float mt = fmaxf(fmaxf(rt[r], rt[R + r]), fmaxf(rt[2 * R + r], rt[3 * R + r]));
+                const float mn = fmaxf(m[r], mt);
+                alpha[q] = (r < rows && mn != -INFINITY) ? fast_exp2(m[r] - mn) : 1.f;   // m = -inf gives 0
+                l[r] *= alpha[q];
+                m[r] = r < rows ? mn : m[r];
+              }
+              if (o_ok) {
+                uint32_t o[CW];
+                tmem_ldw<CW>(o_addr + c * CW, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < CW; ++q) o[q] = __float_as_uint(__uint_as_float(o[q]) * alpha[q]);
+                tmem_stw<CW>(o_addr + c * CW, o);
+              }
+            }
+          }
+          if (o_ok) tmem_wait_st();
+        }
+        // P^T = exp2(s - m) over each row's live keys, bf16/f16, K-major swizzled
+        if (alive) {
+          unsigned char* pt = pbuf + b * C::kQBytes;
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            if (c * CW < rows) {
+              uint32_t raw[CW];
+              if (c == 0) {
+#pragma unroll
+                for (int q = 0; q < CW; ++q) raw[q] = keep[q];
+              } else {
+                tmem_ldw<CW>(s_addr + c * CW, raw);
+                tmem_wait_ld();
+              }
+              uint16_t e16[CW];
+#pragma unroll
+              for (int q = 0; q < CW; ++q) {
+                const int r = c * CW + q;
+                const float e = ((live_rows >> r) & 1ull) ? fast_exp2(__uint_as_float(raw[q]) * scale - m[r]) : 0.f;
+                l[r] += e;
+                e16[q] = Elem<T>::from_float(e);
+              }
+#pragma unroll
+              for (int q = 0; q < CW; ++q)
+                if (c * CW + q < rows) *reinterpret_cast<uint16_t*>(pt + swz(C::kQHalf, c * CW + q, kk)) = e16[q];
+            }
+          }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[b]);
+        if (j == 0 && pend_k >= 0) {
+          // the previous task's epilogue: its P.V has had this tile to finish
+          epilogue(pend_k, pend_g, (qi - 1) & 1);
+          pend_k = -1;
+        }
+      }
+      // this task's row sums and maxima, for its deferred epilogue
+      {
+        const int b = qi & 1;
+        float* sl = suml + b * 4 * R;
+        if constexpr (R <= 16) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            if (r < rows) {
+              const float s = warp_sum(l[r]);
+              if (lane == 0) sl[warp * R + r] = s;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < R / 32; ++c) {
+            float v[32];
+#pragma unroll
+            for (int q = 0; q < 32; ++q) v[q] = l[c * 32 + q];
+            sl[warp * R + c * 32 + lane] = warp_transpose_sum32(v, lane);
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          if (kk == r && r < rows) mfin[b * R + r] = m[r];
+      }
+      pend_k = k;
+      pend_g = g - 1;
+      ++qi;
+    }
+    if (pend_k >= 0) epilogue(pend_k, pend_g, (qi - 1) & 1);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
+  }
+}
+
+template <typename T, int R>
+cudaError_t launch_r(const SegParams& p, cudaStream_t stream) {
+  CUtensorMap tk, tv;
+  if (!make_pool_map(&tk, p.k, p.pool_tokens, p.num_kv_heads, kBoxRows) ||
+      !make_pool_map(&tv, p.v, p.pool_tokens, p.num_kv_heads, kBoxRows))
+    return cudaErrorInvalidValue;
+  auto kernel = seg_kn_kernel<T, R>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(KnCfg<R>::alloc));
+    if (err != cudaSuccess) return err;
+    configured = true;
+  }
+  kernel<<<p.kn_ctas, kThreads, KnCfg<R>::alloc, stream>>>(p, tk, tv);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_t(const SegParams& p, int rows, cudaStream_t stream) {
+  if (rows <= 4) return launch_r<T, 4>(p, stream);
+  if (rows <= 8) return launch_r<T, 8>(p, stream);
+  if (rows <= 16) return launch_r<T, 16>(p, stream);
+  if (rows <= 32) return launch_r<T, 32>(p, stream);
+  if (rows <= 64) return launch_r<T, 64>(p, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t launch_seg_kn(const SegParams& p, int rows, int dtype, cudaStream_t stream) {
+  if (p.num_kn_tasks <= 0 || p.kn_ctas <= 0) return cudaSuccess;
+  if (dtype == TA_DTYPE_BF16) return launch_t<__nv_bfloat16>(p, rows, stream);
+  if (dtype == TA_DTYPE_F16) return launch_t<__half>(p, rows, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ta

@@ -72,24 +72,21 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
   const int head = blockIdx.y;
   const int G = p.group;
 
-  const int job = p.small_tasks[2 * task];
+  const int piece = p.small_tasks[2 * task];
   const int tile = p.small_tasks[2 * task + 1];
-  if (job < 0 || job >= p.num_jobs) {
+  Piece pc;
+  const int state = resolve_piece(p, piece, pc);
+  const int r0 = tile * 16;
+  const int rows = state == PIECE_SKIP ? 0 : min(R, pc.nr * G - r0);
+  if (rows <= 0) {
     if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
     return;
   }
-  const int nr = p.qlen[job];
-  int nk = p.klen[job];
-  const int64_t k0 = p.kstart[int64_t(job) * p.kstart_stride];
-  const int r0 = tile * 16;
-  const int rows = min(R, nr * G - r0);
-  const int64_t part_row0 = int64_t(p.slot_base[job]) * G + r0;
-  const bool rows_ok = rows > 0 && part_row0 >= 0 && part_row0 + rows <= int64_t(p.num_partials) * G;
-  if (!rows_ok || nr > p.max_requests || nk < 0 || k0 < 0 || k0 + nk > p.pool_tokens) {
-    if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
-    if (!rows_ok) return;
-    nk = 0;  // rows are addressable: publish an empty partial (O = 0, LSE = -inf)
-  }
+  if (state == PIECE_BAD_KEYS && tid == 0) set_status(p.status, TA_ERR_BOUNDS);
+  const int job = pc.job;
+  const int nk = pc.nk;
+  const int64_t k0 = pc.k0;
+  const int64_t part_row0 = pc.slot * G + r0;
   const int nchunks = (nk + kChunk - 1) / kChunk;
   const uint16_t* kbase = p.k + (int64_t(head) * p.pool_tokens + k0) * D;
   const uint16_t* vbase = p.v + (int64_t(head) * p.pool_tokens + k0) * D;

@@ -40,11 +40,8 @@
 //
 // The reference's _segment (kernels.py:8-55) computes the same partial O / LSE
 // with Triton tiles of 64 query rows x 64 keys.
-#include <cstring>
-#include <mutex>
-
-#include "ta_common.cuh"
 #include "ta_kernels.cuh"
+#include "tc_common.cuh"
 
 namespace ta {
 
@@ -85,106 +82,11 @@ enum Bar {
   K_FULL = 0, K_EMPTY = 2, V_FULL = 4, V_EMPTY = 6, S_FULL = 8, P_FULL = 10, PV_DONE = 12, Q_FULL = 14, V_TAIL = 15
 };
 
-// ---- UMMA descriptors -------------------------------------------------------
-// Shared-memory matrix descriptor (sm_100): start>>4 [0,14), LBO>>4 [16,30),
-// SBO>>4 [32,46), version 1 [46,48), base offset 0, layout [61,64) = 2 (128B swizzle).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= uint64_t((addr >> 4) & 0x3fff);
-  d |= uint64_t((lbo >> 4) & 0x3fff) << 16;
-  d |= uint64_t((sbo >> 4) & 0x3fff) << 32;
-  d |= uint64_t(1) << 46;
-  d |= uint64_t(2) << 61;
-  return d;
-}
-
-// Instruction descriptor, kind::f16: D f32, A/B f16 (0) or bf16 (1), K-major
-// A, M = 128, N = 128; b_mn_major selects an N-contiguous B (the V tile).
+// Instruction descriptor of this kernel's MMAs: M = 128 query rows, N = 128
+// (keys for S, head dims for P.V), K-major A; b_mn_major selects an
+// N-contiguous B (the V tile).
 __host__ __device__ constexpr uint32_t instr_desc(uint32_t ab_format, uint32_t b_mn_major) {
-  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (b_mn_major << 16) | ((uint32_t(kKeys) >> 3) << 17) |
-         ((uint32_t(kRows) >> 4) << 24);
-}
-
-// D (TMEM) (+)= A (smem) * B (smem)
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-
-// D (TMEM) (+)= A (TMEM) * B (smem)
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// Named barrier among `count` threads (id 0 is __syncthreads).
-__device__ __forceinline__ void named_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-#define TA_REGS32(r) "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), \
-  "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),                \
-  "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),              \
-  "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-#define TA_VALS32(r) "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), \
-  "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),                \
-  "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),              \
-  "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-
-// 32 consecutive 32-bit columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : TA_REGS32(r)
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
-      ::"r"(taddr), TA_VALS32(r));
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// Bounded wait whose outcome is the same for every lane of the warp, so the
-// warp-collective tcgen05 instructions that follow never run diverged.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
-  const bool ok = mbar_wait(bar, parity, status);
-  return __all_sync(0xffffffffu, ok);
-}
-
-__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int x, int y, int z) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
-      "[%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
+  return umma_idesc(ab_format, 0, b_mn_major, kRows, kKeys);
 }
 
 // Maximum of 64 values as a balanced tree (short dependency chains).
@@ -195,32 +97,6 @@ __device__ __forceinline__ float max64(const float (&s)[kHalfCols]) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], fmaxf(fmaxf(s[i + 32], s[i + 40]), fmaxf(s[i + 48], s[i + 56])));
   return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
-}
-
-// Packed pairs of f32 (sm_100 FFMA2 / FADD2): half the issue slots.
-union F2 {
-  unsigned long long u;
-  float2 f;
-};
-__device__ __forceinline__ F2 ffma2(F2 a, F2 b, F2 c) {
-  F2 d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.u) : "l"(a.u), "l"(b.u), "l"(c.u));
-  return d;
-}
-__device__ __forceinline__ F2 fadd2(F2 a, F2 b) {
-  F2 d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d.u) : "l"(a.u), "l"(b.u));
-  return d;
-}
-__device__ __forceinline__ F2 fsub2(F2 a, F2 b) {
-  F2 d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d.u) : "l"(a.u), "l"(b.u));
-  return d;
-}
-__device__ __forceinline__ F2 splat(float x) {
-  F2 r;
-  r.f = make_float2(x, x);
-  return r;
 }
 
 // 2^x for a pair on the FMA pipe: x = n + f with n = round(x) via the
@@ -265,25 +141,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int task = blockIdx.x, head = blockIdx.y;
   const int G = p.group;
 
-  const int job = p.tc_tasks[2 * task];
+  const int piece = p.tc_tasks[2 * task];
   const int pair = p.tc_tasks[2 * task + 1];
-  if (job < 0 || job >= p.num_jobs) {
+  Piece pc;
+  const int state = resolve_piece(p, piece, pc);
+  const int r0 = pair * 2 * kRows;
+  const int rows = state == PIECE_SKIP ? 0 : min(2 * kRows, pc.nr * G - r0);   // rows of this pair
+  if (rows <= 0) {
     if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
     return;
   }
-  const int nr = p.qlen[job];
-  int nk = p.klen[job];
-  const int64_t k0 = p.kstart[int64_t(job) * p.kstart_stride];
-  const int r0 = pair * 2 * kRows;
-  const int rows = min(2 * kRows, nr * G - r0);            // rows of this pair
+  if (state == PIECE_BAD_KEYS && tid == 0) set_status(p.status, TA_ERR_BOUNDS);
+  const int job = pc.job;
+  const int nk = pc.nk;
+  const int64_t k0 = pc.k0;
   const int ntile = rows > kRows ? 2 : 1;                  // tile B present?
-  const int64_t part_row0 = int64_t(p.slot_base[job]) * G + r0;
-  const bool rows_ok = rows > 0 && part_row0 >= 0 && part_row0 + rows <= int64_t(p.num_partials) * G;
-  if (!rows_ok || nr > p.max_requests || nk < 0 || k0 < 0 || k0 + nk > p.pool_tokens || k0 > INT32_MAX - kKeys) {
-    if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
-    if (!rows_ok) return;
-    nk = 0;
-  }
+  const int64_t part_row0 = pc.slot * G + r0;
   const int ntiles = (nk + kKeys - 1) / kKeys;
   const int64_t head_rows = int64_t(head) * p.num_partials * G;
 
@@ -599,42 +472,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// ---- host side: tensor maps through the driver entry point -------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  });
-  return fn;
-}
-
-// Pool [heads, tokens, 128] of 16-bit elements; box = 64 columns x 128 rows x 1 head.
-bool make_pool_map(CUtensorMap* map, const void* base, int64_t tokens, int heads) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn || tokens <= 0) return false;
-  cuuint64_t dims[3] = {cuuint64_t(kDim), cuuint64_t(tokens), cuuint64_t(heads)};
-  cuuint64_t strides[2] = {cuuint64_t(kDim) * 2, cuuint64_t(tokens) * kDim * 2};
-  cuuint32_t box[3] = {64, cuuint32_t(kKeys), 1};
-  cuuint32_t elem[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, elem,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 template <typename T>
 cudaError_t launch_typed(const SegParams& p, int num_tasks, cudaStream_t stream) {
   CUtensorMap tk, tv;
-  if (!make_pool_map(&tk, p.k, p.pool_tokens, p.num_kv_heads) || !make_pool_map(&tv, p.v, p.pool_tokens, p.num_kv_heads))
+  if (!make_pool_map(&tk, p.k, p.pool_tokens, p.num_kv_heads, kKeys) ||
+      !make_pool_map(&tv, p.v, p.pool_tokens, p.num_kv_heads, kKeys))
     return cudaErrorInvalidValue;
   auto kernel = seg_tc_kernel<T>;
   static bool configured = false;

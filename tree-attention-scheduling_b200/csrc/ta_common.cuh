@@ -1,8 +1,8 @@
 // Shared device helpers for the tree-attention kernels (sm_100a only).
 //
-// Every wait on an mbarrier is bounded: after TA_SPIN_LIMIT polls the waiting
-// thread records TA_ERR_TIMEOUT in the call's status word and gives up, so a
-// lost completion can never hang the GPU.  Index checks on plan metadata record
+// Every wait on an mbarrier is bounded: after about a second the waiting thread
+// records TA_ERR_TIMEOUT in the call's status word and gives up, so a lost
+// completion can never hang the GPU.  Index checks on plan metadata record
 // TA_ERR_BOUNDS and skip the access instead of trapping.
 #pragma once
 
@@ -20,10 +20,10 @@
 
 namespace ta {
 
-// Polls of mbarrier.try_wait before a wait is declared lost.  Each poll may
-// suspend the thread for a hardware-chosen interval; 2^26 polls is on the order
-// of seconds, far above any legitimate wait in these kernels.
-constexpr uint32_t TA_SPIN_LIMIT = 1u << 26;
+// A wait on an mbarrier is declared lost after TA_WAIT_NS nanoseconds of the
+// global timer (about a second: far above any legitimate wait in these
+// kernels, short enough that a lost completion ends the kernel quickly).
+constexpr uint64_t TA_WAIT_NS = 1000000000ull;
 
 __device__ __forceinline__ void set_status(int32_t* status, int32_t bit) {
   if (status) atomicOr(status, bit);
@@ -121,11 +121,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Bounded wait for phase `parity` of `bar`.  Returns false (and records the
-// timeout) if the phase never completed.
+// timeout) if the phase did not complete within TA_WAIT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
-  for (uint32_t i = 0; i < TA_SPIN_LIMIT; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - start > TA_WAIT_NS) break;
   }
   set_status(status, TA_ERR_TIMEOUT);
   return false;

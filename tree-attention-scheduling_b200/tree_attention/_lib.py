@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libtree_attn_b200.so")
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 DTYPE_BF16 = 1
 DTYPE_F16 = 2
@@ -37,28 +37,14 @@ EXPORTS = ("ta_abi_version", "ta_error_string", "ta_segment", "ta_merge", "ta_at
 
 class PlanLayout(ctypes.Structure):
     """Mirror of ``ta_plan_layout``."""
-    _fields_ = [
-        ("num_jobs", ctypes.c_int32),
-        ("max_requests", ctypes.c_int32),
-        ("max_slots", ctypes.c_int32),
-        ("num_requests", ctypes.c_int32),
-        ("num_partials", ctypes.c_int32),
-        ("num_small_tasks", ctypes.c_int32),
-        ("num_tc_tasks", ctypes.c_int32),
-        ("small_class_end", ctypes.c_int32 * 3),
-        ("small_max_keys", ctypes.c_int32),
-        ("kstart_stride", ctypes.c_int32),
-        ("off_qids", ctypes.c_int32),
-        ("off_kstart", ctypes.c_int32),
-        ("off_qlen", ctypes.c_int32),
-        ("off_klen", ctypes.c_int32),
-        ("off_slots", ctypes.c_int32),
-        ("off_counts", ctypes.c_int32),
-        ("off_slot_base", ctypes.c_int32),
-        ("off_cslots", ctypes.c_int32),
-        ("off_small_tasks", ctypes.c_int32),
-        ("off_tc_tasks", ctypes.c_int32),
-    ]
+    _fields_ = [(name, ctypes.c_int32) for name in (
+        "num_jobs", "max_requests", "max_slots", "num_requests", "num_pieces", "num_partials", "max_pslots",
+        "num_small_tasks", "num_tc_tasks", "num_kn_tasks", "num_kn_segs", "kn_ctas", "kn_rows")]
+    _fields_ += [("small_class_end", ctypes.c_int32 * 3)]
+    _fields_ += [(name, ctypes.c_int32) for name in (
+        "small_max_keys", "kstart_stride", "off_qids", "off_kstart", "off_qlen", "off_klen", "off_slots",
+        "off_counts", "off_pieces", "off_pcounts", "off_cslots", "off_small_tasks", "off_tc_tasks",
+        "off_kn_offsets", "off_kn_tasks", "off_kn_segs")]
 
 
 def describe_status(code):

@@ -35,10 +35,15 @@ import torch
 from . import _lib
 from .schedule import Job, Plan, physical_jobs
 
-# Query rows a small-group (SIMT) task covers; larger jobs go to the tensor-core
-# kernel in tiles of TC_ROWS rows when it supports the shape.
-SMALL_ROWS = 16
+# Routing of a job's query rows (requests x GQA group) for head_dim 128:
+# up to KN_ROWS rows run on the persistent keys-in-lanes tcgen05 kernel
+# (queries are the MMA N dimension), more rows on the query-tile tcgen05 kernel
+# in pairs of 128-row tiles (TC_ROWS).  Other head sizes use the SIMT kernel in
+# tiles of SMALL_ROWS rows.
+KN_ROWS = 64
 TC_ROWS = 256
+SMALL_ROWS = 16
+KEY_TILE = 128
 # Reference sort key: jobs with more than 16 query rows run in the second phase
 # (kernels.py:109-110).  Kept verbatim so the metadata is bit-identical.
 _REF_SMALL_ROWS = 16
@@ -74,10 +79,11 @@ class PreparedPlan:
     # -- B200 additions ------------------------------------------------------
     metadata: torch.Tensor = None
     layout: _lib.PlanLayout = None
-    slot_base: torch.Tensor = None
+    pieces: torch.Tensor = None
     cslots: torch.Tensor = None
     small_tasks: torch.Tensor = None
     tc_tasks: torch.Tensor = None
+    kn_tasks: torch.Tensor = None
     status: torch.Tensor = None
     num_kv_heads: int = 0
     host_arrays: dict = field(default_factory=dict)
@@ -87,11 +93,148 @@ def _small_class(rows):
     return 0 if rows <= 4 else (1 if rows <= 8 else 2)
 
 
-def build_metadata(jobs, num_requests, groups, use_tc):
+def _route(rows, use_tc):
+    if not use_tc:
+        return "simt"
+    return "kn" if rows <= KN_ROWS else "tc"
+
+
+def _tiles(keys):
+    return max(1, -(-keys // KEY_TILE))
+
+
+def split_pieces(jobs, groups, heads, use_tc, sms, no_split_from=None):
+    """Cut jobs into execution pieces ``(job, key_offset, keys)`` so the kernels fill the GPU.
+
+    A piece is a contiguous key range of one job with its own partial slots;
+    the merge combines a request's partials across pieces exactly as across
+    jobs, so splitting changes the work distribution, never the result beyond
+    float rounding.  Keys-in-lanes jobs are cut so no piece holds more than
+    about half a CTA's share of all key tiles; query-tile jobs are cut while
+    their CTAs still fit one wave on ``sms`` SMs.  Jobs whose first position is
+    at or past ``no_split_from`` (the growing decode tails) stay whole.
+    """
+    n = len(jobs)
+    rows = [len(j.requests) * groups for j in jobs]
+    route = [_route(r, use_tc) for r in rows]
+    keys = [len(j.tokens) for j in jobs]
+    splittable = [no_split_from is None or j.tokens[0] < no_split_from for j in jobs]
+    count = [1] * n
+
+    kn = [i for i in range(n) if route[i] == "kn"]
+    if kn:
+        total = sum(_tiles(keys[i]) for i in kn) * heads
+        cap = max(2, -(-total // (2 * sms)))
+        for i in kn:
+            if splittable[i] and _tiles(keys[i]) > cap:
+                count[i] = -(-_tiles(keys[i]) // cap)
+
+    tc = [i for i in range(n) if route[i] == "tc"]
+    if tc:
+        pairs = {i: -(-rows[i] // TC_ROWS) * heads for i in tc}
+        ctas = sum(pairs.values())
+        while True:
+            best = max((i for i in tc if splittable[i] and _tiles(keys[i]) / (count[i] + 1) >= 2
+                        and ctas + pairs[i] <= sms),
+                       key=lambda i: _tiles(keys[i]) / count[i], default=None)
+            if best is None:
+                break
+            count[best] += 1
+            ctas += pairs[best]
+
+    pieces = []
+    for i in range(n):
+        tiles = _tiles(keys[i])
+        per = -(-tiles // count[i]) * KEY_TILE
+        offset = 0
+        while True:
+            take = min(per, keys[i] - offset)
+            pieces.append((i, offset, take))
+            offset += take
+            if offset >= keys[i]:
+                break
+    return pieces, route, rows
+
+
+KN_BOX = 32          # keys-in-lanes TMA box height: packed segments start on 32-key boundaries
+KN_PACK_ROWS = 16    # query rows of a packed tile
+KN_PACK_SEGS = 4     # segments of a packed tile
+
+
+def pack_segments(items):
+    """Group keys-in-lanes segments into tasks.
+
+    ``items`` are ``(head, rows, slot, k0, keys, job_flags)``.  A segment of more
+    than one 128-key tile is a task of its own; shorter ones are packed, best
+    fit by their 32-key-rounded span, into tiles of 128 keys, at most
+    KN_PACK_SEGS segments and KN_PACK_ROWS query rows each (a segment of more
+    rows stays alone).  Returns a list of tasks, each a list of items.
+    """
+    tasks, open_bins = [], {32: [], 64: [], 96: []}    # remaining span -> bins
+    packable = []
+    for item in items:
+        span = -(-item[4] // KN_BOX) * KN_BOX
+        if item[4] > KEY_TILE or span >= KEY_TILE or item[1] > KN_PACK_ROWS // 2:
+            tasks.append([item])
+        else:
+            packable.append((span, item))
+    packable.sort(key=lambda x: -x[0])
+    for span, item in packable:
+        placed = False
+        for free in (32, 64, 96):
+            if free < span:
+                continue
+            for b, (segs, used_rows) in enumerate(open_bins[free]):
+                if used_rows + item[1] <= KN_PACK_ROWS and len(segs) < KN_PACK_SEGS:
+                    open_bins[free].pop(b)
+                    segs.append(item)
+                    left = free - span
+                    if left and len(segs) < KN_PACK_SEGS:
+                        open_bins[left].append((segs, used_rows + item[1]))
+                    else:
+                        tasks.append(segs)
+                    placed = True
+                    break
+                break                     # rows are uniform enough: only the first bin is tried
+            if placed:
+                break
+        if not placed:
+            left = KEY_TILE - span
+            if left:
+                open_bins[left].append(([item], item[1]))
+            else:
+                tasks.append([item])
+    for free in (32, 64, 96):
+        tasks.extend(segs for segs, _ in open_bins[free])
+    return tasks
+
+
+def assign_lpt(costs, bins):
+    """Longest-processing-time assignment of tasks to ``bins`` persistent CTAs.
+
+    Returns (offsets [bins + 1], order): CTA b runs ``order[offsets[b]:offsets[b + 1]]``.
+    """
+    import heapq
+    heap = [(0, b) for b in range(bins)]
+    lists = [[] for _ in range(bins)]
+    for task in sorted(range(len(costs)), key=lambda t: -costs[t]):
+        load, b = heapq.heappop(heap)
+        lists[b].append(task)
+        heapq.heappush(heap, (load + costs[task], b))
+    offsets = np.zeros(bins + 1, dtype=np.int32)
+    np.cumsum([len(x) for x in lists], out=offsets[1:])
+    order = np.array([t for x in lists for t in x], dtype=np.int32)
+    return offsets, order
+
+
+def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_split_from=None):
     """Host-side metadata of a sorted physical job list (numpy int32 arrays).
 
     Returns the reference arrays (qids, kids, qlen, klen, slots, counts) and the
-    B200 arrays (slot_base, cslots, small_tasks, tc_tasks, small_class_end).
+    B200 arrays: execution pieces [P, 4] (job, key offset, keys, first partial
+    slot), per-request partial counts and slots over pieces, SIMT tasks (piece,
+    16-row tile) in three row classes, query-tile tasks (piece, 256-row pair)
+    and the keys-in-lanes tasks (headers in persistent-CTA order, segment records).
     """
     njobs = len(jobs)
     maxr = max(len(j.requests) for j in jobs)
@@ -101,54 +244,92 @@ def build_metadata(jobs, num_requests, groups, use_tc):
     kids = np.zeros((njobs, maxk), dtype=np.int32)
     qlen = np.fromiter((len(j.requests) for j in jobs), dtype=np.int32, count=njobs)
     klen = np.fromiter((len(j.tokens) for j in jobs), dtype=np.int32, count=njobs)
-    slot_base = np.zeros(njobs, dtype=np.int32)
-    if njobs > 1:
-        np.cumsum(qlen[:-1], out=slot_base[1:])
     per_request = [[] for _ in range(num_requests)]
-    per_request_compact = [[] for _ in range(num_requests)]
     for i, job in enumerate(jobs):
         qids[i, :len(job.requests)] = job.requests
         if contiguous_k:
             kids[i, 0] = job.tokens[0]
         else:
             kids[i, :len(job.tokens)] = job.tokens
-        base = int(slot_base[i])
         for j, r in enumerate(job.requests):
             per_request[r].append(i * maxr + j)
-            per_request_compact[r].append(base + j)
     maxs = max(map(len, per_request))
     slots = np.zeros((num_requests, maxs), dtype=np.int32)
-    cslots = np.zeros((num_requests, maxs), dtype=np.int32)
     for r in range(num_requests):
         slots[r, :len(per_request[r])] = per_request[r]
-        cslots[r, :len(per_request_compact[r])] = per_request_compact[r]
     counts = np.fromiter((len(s) for s in per_request), dtype=np.int32, count=num_requests)
+
+    piece_list, route, rows = split_pieces(jobs, groups, heads, use_tc, sms, no_split_from)
+    npieces = len(piece_list)
+    pieces = np.zeros((npieces, 4), dtype=np.int32)
+    per_request_p = [[] for _ in range(num_requests)]
+    slot = 0
+    for p, (i, offset, take) in enumerate(piece_list):
+        pieces[p] = (i, offset, take, slot)
+        for j, r in enumerate(jobs[i].requests):
+            per_request_p[r].append(slot + j)
+        slot += len(jobs[i].requests)
+    maxp = max(map(len, per_request_p))
+    cslots = np.zeros((num_requests, maxp), dtype=np.int32)
+    for r in range(num_requests):
+        cslots[r, :len(per_request_p[r])] = per_request_p[r]
+    pcounts = np.fromiter((len(s) for s in per_request_p), dtype=np.int32, count=num_requests)
 
     small = [[], [], []]
     tc = []
-    for i in range(njobs):
-        rows = int(qlen[i]) * groups
-        if rows <= SMALL_ROWS:
-            small[_small_class(rows)].append((i, 0))
-        elif use_tc:
-            tc.extend((i, t) for t in range(ceil(rows / TC_ROWS)))
+    items = []          # keys-in-lanes segments: one per (piece, KV head)
+    for p, (i, offset, take) in enumerate(piece_list):
+        if route[i] == "kn":
+            growing = int(no_split_from is not None and jobs[i].tokens[0] >= no_split_from)
+            for h in range(heads):
+                items.append((h, rows[i], int(pieces[p, 3]), jobs[i].tokens[0] + offset, take, i | (growing << 30)))
+        elif route[i] == "tc":
+            tc.extend((p, t) for t in range(ceil(rows[i] / TC_ROWS)))
         else:
-            for t in range(ceil(rows / SMALL_ROWS)):
-                small[_small_class(min(SMALL_ROWS, rows - t * SMALL_ROWS))].append((i, t))
+            for t in range(ceil(rows[i] / SMALL_ROWS)):
+                small[_small_class(min(SMALL_ROWS, rows[i] - t * SMALL_ROWS))].append((p, t))
     class_end = np.cumsum([len(c) for c in small]).astype(np.int32)
-    small_max_keys = max((int(klen[i]) for c in small for i, _ in c), default=0)
+    small_max_keys = max((piece_list[p][2] for c in small for p, _ in c), default=0)
     small_tasks = np.array([t for c in small for t in c], dtype=np.int32).reshape(-1, 2)
     tc_tasks = np.array(tc, dtype=np.int32).reshape(-1, 2)
+    tasks = pack_segments(items)
+    kn_ctas = min(sms, len(tasks))
+    segs = []
+    headers = []
+    costs = []
+    for task in tasks:
+        headers.append((len(segs), len(task), 0, 0))
+        row0, kt = 0, 0
+        for h, r, first_slot, k0, keys, job in task:
+            segs.append((h, row0, r, first_slot, k0, kt if len(task) > 1 else 0, keys, job))
+            row0 += r
+            kt += -(-keys // KN_BOX) * KN_BOX
+        costs.append(_tiles(max(s[4] for s in task)) + 1)
+    kn_rows = max((sum(s[1] for s in task) for task in tasks), default=0)
+    if tasks:
+        kn_offsets, order = assign_lpt(costs, kn_ctas)
+        kn_tasks = np.array(headers, dtype=np.int32)[order]
+    else:
+        kn_offsets, kn_tasks = np.zeros(1, dtype=np.int32), np.zeros((0, 4), dtype=np.int32)
+    kn_segs = np.array(segs, dtype=np.int32).reshape(-1, 8)
     return dict(qids=qids, kids=kids, qlen=qlen, klen=klen, slots=slots, counts=counts,
-                slot_base=slot_base, cslots=cslots, small_tasks=small_tasks, tc_tasks=tc_tasks,
-                small_class_end=class_end, small_max_keys=small_max_keys, contiguous_k=contiguous_k,
-                num_partials=int(qlen.sum()))
+                pieces=pieces, pcounts=pcounts, cslots=cslots, small_tasks=small_tasks, tc_tasks=tc_tasks,
+                kn_offsets=kn_offsets, kn_tasks=kn_tasks, kn_segs=kn_segs, small_class_end=class_end,
+                small_max_keys=small_max_keys, kn_ctas=kn_ctas, kn_rows=kn_rows, contiguous_k=contiguous_k,
+                num_partials=slot)
 
 
-_ORDER = ("qids", "kids", "qlen", "klen", "slots", "counts", "slot_base", "cslots", "small_tasks", "tc_tasks")
+_ORDER = ("qids", "kids", "qlen", "klen", "slots", "counts", "pieces", "pcounts", "cslots", "small_tasks",
+          "tc_tasks", "kn_offsets", "kn_tasks", "kn_segs")
 
 
-def prepare(plan, q, num_kv_heads=None):
+def _sm_count(device):
+    if device.type == "cuda" and torch.cuda.is_available():
+        return torch.cuda.get_device_properties(device).multi_processor_count
+    return 148
+
+
+def prepare(plan, q, num_kv_heads=None, _no_split_from=None):
     """Materialise ``plan`` for queries shaped like ``q`` ``[NREQ, HQ, D]`` (reference kernels.py:103-141).
 
     ``num_kv_heads`` defaults to ``plan.settings["kvheads"]``; a KV-head shard
@@ -168,13 +349,18 @@ def prepare(plan, q, num_kv_heads=None):
             raise ValueError("Plan contains an empty job")
         if any(r < 0 or r >= nreq for r in job.requests):
             raise ValueError("Plan references a request outside the query batch")
-    meta = build_metadata(jobs, nreq, groups, tc_supported(dim, q.dtype))
+    meta = build_metadata(jobs, nreq, groups, tc_supported(dim, q.dtype), kvheads, _sm_count(q.device),
+                          _no_split_from)
     if not meta["contiguous_k"]:
         raise ValueError("Physical jobs must read contiguous KV positions")
 
     offsets, pieces, offset = {}, [], 0
     for name in _ORDER:
         array = meta[name]
+        pad = -offset % 4                 # every array starts on a 16-byte boundary
+        if pad:
+            pieces.append(np.zeros(pad, dtype=np.int32))
+            offset += pad
         offsets[name] = offset
         pieces.append(array.ravel())
         offset += array.size
@@ -189,9 +375,15 @@ def prepare(plan, q, num_kv_heads=None):
     layout.max_requests = meta["qids"].shape[1]
     layout.max_slots = meta["slots"].shape[1]
     layout.num_requests = nreq
+    layout.num_pieces = meta["pieces"].shape[0]
     layout.num_partials = meta["num_partials"]
+    layout.max_pslots = meta["cslots"].shape[1]
     layout.num_small_tasks = meta["small_tasks"].shape[0]
     layout.num_tc_tasks = meta["tc_tasks"].shape[0]
+    layout.num_kn_tasks = meta["kn_tasks"].shape[0]
+    layout.num_kn_segs = meta["kn_segs"].shape[0]
+    layout.kn_ctas = meta["kn_ctas"]
+    layout.kn_rows = meta["kn_rows"]
     for i in range(3):
         layout.small_class_end[i] = int(meta["small_class_end"][i])
     layout.small_max_keys = meta["small_max_keys"]
@@ -202,10 +394,14 @@ def prepare(plan, q, num_kv_heads=None):
     layout.off_klen = offsets["klen"]
     layout.off_slots = offsets["slots"]
     layout.off_counts = offsets["counts"]
-    layout.off_slot_base = offsets["slot_base"]
+    layout.off_pieces = offsets["pieces"]
+    layout.off_pcounts = offsets["pcounts"]
     layout.off_cslots = offsets["cslots"]
     layout.off_small_tasks = offsets["small_tasks"]
     layout.off_tc_tasks = offsets["tc_tasks"]
+    layout.off_kn_offsets = offsets["kn_offsets"]
+    layout.off_kn_tasks = offsets["kn_tasks"]
+    layout.off_kn_segs = offsets["kn_segs"]
 
     rows = meta["num_partials"] * groups
     contiguous_q = all(j.requests[-1] - j.requests[0] + 1 == len(j.requests) for j in jobs)
@@ -215,8 +411,8 @@ def prepare(plan, q, num_kv_heads=None):
         torch.empty((kvheads, rows, dim), device=device, dtype=torch.float32),
         torch.empty((kvheads, rows), device=device, dtype=torch.float32),
         torch.empty_like(q),
-        metadata=metadata, layout=layout, slot_base=views["slot_base"], cslots=views["cslots"],
-        small_tasks=views["small_tasks"], tc_tasks=views["tc_tasks"],
+        metadata=metadata, layout=layout, pieces=views["pieces"], cslots=views["cslots"],
+        small_tasks=views["small_tasks"], tc_tasks=views["tc_tasks"], kn_tasks=views["kn_tasks"],
         status=torch.zeros(1, device=device, dtype=torch.int32), num_kv_heads=kvheads,
         host_arrays=meta)
 
@@ -288,7 +484,7 @@ class CachedDecodePlan:
                                        prefix_tokens + (r + 1) * max_new_tokens)))
                  for r in range(q.shape[0])]
         plan = Plan(prefix_plan.jobs + tails, prefix_plan.method, prefix_plan.estimated_us, prefix_plan.settings)
-        self.prepared = prepare(plan, q, num_kv_heads)
+        self.prepared = prepare(plan, q, num_kv_heads, _no_split_from=prefix_tokens)
         ordered = self.prepared.jobs
         tail_ids = [i for i, job in enumerate(ordered) if job.tokens[0] >= prefix_tokens]
         self.tail_indices = torch.tensor(tail_ids, device=q.device, dtype=torch.int32)
