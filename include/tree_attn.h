@@ -41,12 +41,14 @@
  *   kn_offsets  [kn_ctas + 1]               task range of each persistent CTA of the
  *                                           keys-in-lanes tcgen05 kernel
  *   kn_tasks    [num_kn_tasks, 4]           its task headers: first segment, segments, 0, 0
- *   kn_segs     [num_kn_segs, 8]            segments: KV head, first query row in the
+ *   kn_segs     [num_kn_segs, 12]           segments: KV head, first query row in the
  *                                           task, query rows, first partial slot, first
  *                                           pool position, first key of its slot in the
  *                                           tile, keys, job | growing << 30 (growing: keys
- *                                           = min(keys, klen[job]), a decode tail); a task
- *                                           of several segments is one 128-key tile
+ *                                           = min(keys, klen[job]), a decode tail), first
+ *                                           request if the job's requests are contiguous
+ *                                           (else -1), 0, 0, 0; a task of several
+ *                                           segments is one 128-key tile
  * Every array starts at a multiple of 4 int32 (16 bytes).  Partial slot s of a
  * piece holds query rows s*G .. s*G+G-1 (one request).
  *

@@ -75,11 +75,13 @@ def check_b200_arrays(p, groups, heads=None):
     for first, nseg, _, _ in meta["kn_tasks"]:
         assert 1 <= nseg <= kernels.KN_PACK_SEGS
         row0 = kt = 0
-        for head, r0, rows, slot, k0, seg_kt, keys, jobf in segs[first:first + nseg]:
+        for head, r0, rows, slot, k0, seg_kt, keys, jobf, q0, _, _, _ in segs[first:first + nseg]:
             job, growing = int(jobf) & 0x3FFFFFFF, int(jobf) >> 30
             pc = slot_piece[int(slot)]
             assert pieces[pc, 0] == job and keys == pieces[pc, 2] and rows == qlen[job] * groups
             assert k0 == p.jobs[job].tokens[0] + pieces[pc, 1] and growing in (0, 1)
+            reqs = p.jobs[job].requests
+            assert q0 == (reqs[0] if reqs[-1] - reqs[0] + 1 == len(reqs) else -1)
             assert r0 == row0 and (nseg == 1 and seg_kt == 0 or seg_kt == kt)
             if nseg > 1:
                 assert keys <= kernels.KEY_TILE
@@ -211,7 +213,7 @@ def test_packing_shares_tiles_between_short_segments():
     assert p.layout.kn_rows == 8
     check_b200_arrays(p, 4)
     # mixed spans and rows never exceed a tile
-    items = [(h, 4 * (1 + (i % 2)), i, 1000 * i, 1 + (i * 37) % 200, i) for i in range(60) for h in range(2)]
+    items = [(h, 4 * (1 + (i % 2)), i, 1000 * i, 1 + (i * 37) % 200, i, -1) for i in range(60) for h in range(2)]
     for task in kernels.pack_segments(items):
         if len(task) > 1:
             assert sum(-(-it[4] // 32) * 32 for it in task) <= 128 and sum(it[1] for it in task) <= 16

@@ -1,0 +1,114 @@
+"""Qwen3 decode adapter (reference src/tree_attention/qwen.py; check in scripts/check_qwen.py).
+
+Every decode step's logits must match a full-sequence forward of the same
+model over each request's whole token sequence.  On CPU the adapter runs end
+to end with the FP32 oracle standing in for ``attention_matrix`` (the module
+global the reference's model checks also substitute); on a B200 it runs the
+CUDA kernels.
+"""
+import pytest
+import torch
+
+from oracle import attention as oracle
+from tree_attention import CostModel, qwen
+
+transformers = pytest.importorskip("transformers")
+from transformers import Qwen3Config, Qwen3ForCausalLM  # noqa: E402
+
+SEQUENCES = [[1, 2, 3, 4, 5], [1, 2, 3, 8], [1, 2, 3, 4, 5], [7, 8, 9, 10, 11, 12], [1, 2, 3, 4, 5, 6, 9]]
+
+
+def tiny_model(head_dim, heads, kv_heads, dtype, device, seed=2026):
+    torch.manual_seed(seed)
+    config = Qwen3Config(vocab_size=128, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                         num_attention_heads=heads, num_key_value_heads=kv_heads, head_dim=head_dim,
+                         attn_implementation="eager")
+    return Qwen3ForCausalLM(config).to(dtype=dtype, device=device).eval()
+
+
+def reference_logits(model, sequences):
+    with torch.inference_mode():
+        return torch.stack([model(torch.tensor([s], device=model.device), use_cache=False).logits[0, -1]
+                            for s in sequences])
+
+
+def current_paths(decoder):
+    if isinstance(decoder, qwen.CachedPrefixDecoder):
+        base = [tuple(p) for p in decoder.tree.paths]
+        return [path + tuple(decoder.prefix_size + r * decoder.max_new_tokens + t for t in range(decoder.generated))
+                for r, path in enumerate(base)]
+    return [tuple(p) for p in decoder.tree.paths]
+
+
+def oracle_attention(decoder):
+    """Stand-in for attention_matrix: FP32 attention over each request's current path."""
+    def attention(q, kp, vp, prepared, out_lse=None):
+        k = kp.permute(1, 0, 2).float()
+        v = vp.permute(1, 0, 2).float()
+        return oracle.request_attention(q.float(), k, v, current_paths(decoder)).to(q.dtype)
+    return attention
+
+
+@pytest.mark.parametrize("cached", [False, True])
+@pytest.mark.parametrize("prefill", ["shared", "per_request"])
+def test_decoder_matches_full_forward_cpu(cached, prefill, monkeypatch):
+    model = tiny_model(32, 4, 2, torch.float32, "cpu")
+    cls = qwen.CachedPrefixDecoder if cached else qwen.SharedKVDecoder
+    if cached:
+        # the device-side tail update needs a GPU; on CPU the plan's klen is irrelevant to the stand-in
+        monkeypatch.setattr(qwen.CachedDecodePlan, "update", lambda self, n: self.prepared)
+    decoder = cls(model, SEQUENCES, max_new_tokens=4, method="cube")
+    monkeypatch.setattr(qwen, "attention_matrix", oracle_attention(decoder))
+    torch.testing.assert_close(decoder.logits, reference_logits(model, SEQUENCES), atol=1e-4, rtol=1e-4)
+    for _ in range(3):
+        tokens = decoder.logits.argmax(-1).tolist()
+        logits = decoder.step(tokens)
+        torch.testing.assert_close(logits, reference_logits(model, decoder.sequences), atol=1e-4, rtol=1e-4)
+    assert decoder.used == decoder.prefix_size + 3 * len(SEQUENCES)
+    assert decoder.used < sum(map(len, decoder.sequences))          # shared prefixes stored once
+
+
+def test_decoder_capacity_and_shape_errors(monkeypatch):
+    model = tiny_model(32, 4, 2, torch.float32, "cpu")
+    decoder = qwen.SharedKVDecoder(model, SEQUENCES, max_new_tokens=1)
+    monkeypatch.setattr(qwen, "attention_matrix", oracle_attention(decoder))
+    decoder.step([1] * len(SEQUENCES))
+    with pytest.raises(ValueError):
+        decoder.step([1] * len(SEQUENCES))          # exceeds max_new_tokens
+    with pytest.raises(ValueError):
+        decoder.step([1])
+    with pytest.raises(ValueError):
+        qwen.SharedKVDecoder(model, [[1, 2], []])
+    with pytest.raises(ValueError):
+        qwen.SharedKVDecoder(model, SEQUENCES, prefill="nope")
+
+
+def test_shared_prefill_fills_every_position(monkeypatch):
+    model = tiny_model(32, 4, 2, torch.float32, "cpu")
+    a = qwen.SharedKVDecoder(model, SEQUENCES, max_new_tokens=2, prefill="shared")
+    b = qwen.SharedKVDecoder(model, SEQUENCES, max_new_tokens=2, prefill="per_request")
+    n = a.prefix_size
+    for (ka, va), (kb, vb) in zip(a.pools, b.pools):
+        torch.testing.assert_close(ka[:, :n], kb[:, :n], atol=1e-5, rtol=1e-5)
+        torch.testing.assert_close(va[:, :n], vb[:, :n], atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(a.logits, b.logits, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(32, 4, 2), (128, 8, 2), (128, 16, 4)], ids=["d32", "d128g4", "d128g4h16"])
+@pytest.mark.parametrize("cached", [False, True])
+def test_decoder_matches_full_forward_gpu(shape, cached):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    head_dim, heads, kv_heads = shape
+    model = tiny_model(head_dim, heads, kv_heads, torch.float16, "cuda")
+    sequences = [s * 6 for s in SEQUENCES]                # longer shared prefixes: several key tiles
+    cls = qwen.CachedPrefixDecoder if cached else qwen.SharedKVDecoder
+    for method, model_costs in (("cube", CostModel()), ("request", CostModel()), ("cube", CostModel.b200())):
+        decoder = cls(model, sequences, max_new_tokens=3, method=method, cost_model=model_costs)
+        for _ in range(3):
+            tokens = decoder.logits.argmax(-1).tolist()
+            logits = decoder.step(tokens)
+            torch.cuda.synchronize()
+            reference = reference_logits(model, decoder.sequences)
+            torch.testing.assert_close(logits.float(), reference.float(), atol=4e-3, rtol=2e-2)

@@ -40,22 +40,23 @@
 //   warp 4     K producer (ring of STAGES 32 KB tiles)
 //   warp 5     V producer
 //   warp 6     MMA issue (lane 0): waits, zeroes V rows where needed, issues
-//              P.V(g), then S(g+2)
+//              P.V(g), then S(g+3)
 //   warp 7     scheduler: task slots (decode + checks) and Q^T gathers into
 //              two buffers, each released by the MMA's commit after the last S
 //              of its previous task
 //
 // Ordering facts the barrier scheme relies on: MMAs issued by one thread run in
-// issue order, and the issue order is S(0) S(1) PV(0) S(2) PV(1) S(3) ..., so
-// observing S(g) complete implies PV(g-2) has completed.  A parity wait is only
-// correct while its barrier is at most one phase behind, so every per-tile
-// barrier exists twice, by tile parity (S_FULL, P_FULL, PV_DONE): waiting for
-// PV(g) or PV(g-1) after observing S(g) then never aliases.  All waits are
-// bounded and every decision that guards a named barrier is made CTA-uniform
-// first.
+// issue order, and the issue order is S(0) S(1) S(2) PV(0) S(3) PV(1) S(4) ...
+// (S three tiles ahead), so observing S(g) complete implies PV(g-3) has
+// completed, and P^T(g) is rewritten (as P^T(g+3)) only after S(g+3), issued
+// after PV(g).  A parity wait is only correct while its barrier is at most one
+// phase behind, so every per-tile barrier exists three times, by tile index
+// mod 3 (S_FULL, P_FULL, PV_DONE): waiting for PV(g) or PV(g-1) after
+// observing S(g) then never aliases.  All waits are bounded and every decision
+// that guards a named barrier is made CTA-uniform first.
 //
-// TMEM columns: [0, N) and [N, 2N) S^T (by tile parity), [2N, 3N) and
-// [3N, 4N) O^T (by task parity: a task's epilogue runs after the next task's
+// TMEM columns: [0, 3N) three S^T buffers (tile index mod 3), [3N, 5N) two
+// O^T buffers (by task parity: a task's epilogue runs after the next task's
 // first tile, while that task already accumulates into the other buffer).
 // The reference's _segment (kernels.py:8-55) computes the same partial O / LSE
 // per (job, KV head) with Triton tiles of 16 query rows x 64 keys.
@@ -78,12 +79,14 @@ constexpr uint32_t kTileBytes = kKeys * kDim * 2;          // 32 KB
 constexpr uint32_t kHalfBytes = kTileBytes / 2;            // one 64-column swizzled block
 constexpr uint32_t kBoxBytes = kBoxRows * 128;              // one 32-row x 64-column box
 constexpr float kRescaleThreshold = 8.0f;                   // log2 units
+constexpr int kLook = 3;                    // S runs this many tiles ahead of P.V (S / P buffers)
 // task slot words: nseg, ntiles, rows, flags, then per segment
-// head, row0, rows, keys now, first key of its slot, slot keys, job, k0, first partial row
-constexpr int kSegWords = 9;
-constexpr int kTaskWords = 4 + kSegMax * kSegWords;         // 40
+// head, row0, rows, keys now, first key of its slot, slot keys, job, k0, first
+// partial row, first request (-1 unless the job's requests are contiguous)
+constexpr int kSegWords = 10;
+constexpr int kTaskWords = 4 + kSegMax * kSegWords;         // 44
 enum TaskFlag { TASK_BAD = 1, TASK_WRITE = 2 };
-enum SegField { F_HEAD, F_ROW0, F_ROWS, F_NK, F_KT, F_SPAN, F_JOB, F_K0, F_PROW0 };
+enum SegField { F_HEAD, F_ROW0, F_ROWS, F_NK, F_KT, F_SPAN, F_JOB, F_K0, F_PROW0, F_Q0 };
 
 template <int R>
 struct KnCfg {
@@ -95,22 +98,24 @@ struct KnCfg {
   static constexpr uint32_t kQBytes = 2 * kQHalf;           // Q^T or P^T buffer
   static constexpr uint32_t off_k = 0;
   static constexpr uint32_t off_v = off_k + kStages * kTileBytes;
-  static constexpr uint32_t off_q = off_v + kStages * kTileBytes;    // Q^T[2]
-  static constexpr uint32_t off_p = off_q + 2 * kQBytes;              // P^T[2]
-  static constexpr uint32_t off_red = off_p + 2 * kQBytes;            // [2][4][R] tile maxima by tile parity
+  static constexpr int kQBufs = N <= 32 ? 4 : 2;            // Q^T buffers (how far the scheduler runs ahead)
+  static constexpr uint32_t off_q = off_v + kStages * kTileBytes;    // Q^T[kQBufs]
+  static constexpr uint32_t off_p = off_q + kQBufs * kQBytes;         // P^T[kLook]
+  static constexpr uint32_t off_red = off_p + kLook * kQBytes;        // [2][4][R] tile maxima by tile parity
   static constexpr uint32_t off_suml = off_red + 2 * 4 * R * 4;       // [2][4][R] row sums per warp, by task parity
   static constexpr uint32_t off_mfin = off_suml + 2 * 4 * R * 4;      // [2][R] final row maxima, by task parity
   static constexpr uint32_t off_tasks = off_mfin + 2 * R * 4;         // [kTQ][kTaskWords] task slots
-  static constexpr uint32_t off_bar = off_tasks + kTQ * kTaskWords * 4;
-  // k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], q_full[2], pv_done[2],
-  // q_empty[2], task_full[kTQ], task_empty[kTQ]
-  static constexpr int kBars = 4 * kStages + 10 + 2 * kTQ;
+  static constexpr uint32_t off_stage = off_tasks + kTQ * kTaskWords * 4;   // [2][3 * kSegMax] int4 staged segment records
+  static constexpr uint32_t off_bar = off_stage + 2 * 3 * kSegMax * 16;
+  // k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[L], p_full[L], pv_done[L], q_full[QB],
+  // q_empty[QB], task_full[kTQ], task_empty[kTQ]
+  static constexpr int kBars = 4 * kStages + 3 * kLook + 2 * kQBufs + 2 * kTQ;
   static constexpr uint32_t off_tmem = off_bar + kBars * 8;
   static constexpr uint32_t bytes = off_tmem + 16;
   static constexpr uint32_t alloc = bytes + 1024;             // slack to align the base to 1 KB
-  static constexpr uint32_t kTmemCols = N == 16 ? 64 : (N == 32 ? 128 : 256);
+  static constexpr uint32_t kTmemCols = N == 16 ? 128 : (N == 32 ? 256 : 512);   // S^T[kLook] + O^T[2]
   static_assert(alloc <= 227 * 1024, "shared memory budget");
-  static_assert(4 * N <= kTmemCols, "TMEM budget");
+  static_assert((kLook + 2) * N <= kTmemCols, "TMEM budget");
 };
 
 // Header of list entry i: first segment, segment count, 0, 0.
@@ -118,22 +123,21 @@ __device__ __forceinline__ int4 load_header(const SegParams& p, int i) {
   return reinterpret_cast<const int4*>(p.kn_tasks)[i];
 }
 
-// Decode and check list entry `i` into a task slot (one thread).  Segments as
-// the host wrote them (8 int32): KV head, first query row of the tile's N
-// rows, rows, first partial slot, first pool position, first key of its slot
-// in the tile, keys (at most), job | growing << 30.
+// Decode and check one task into a task slot (one thread).  `nseg` and the
+// task's segment records, staged in shared memory, are as the host wrote them
+// (12 int32 each): KV head, first query row of the tile's N rows, rows, first
+// partial slot, first pool position, first key of its slot in the tile, keys
+// (at most), job | growing << 30, first request of the job if its requests
+// are contiguous (else -1), 0, 0, 0.
 template <int R>
-__device__ __noinline__ void decode_task(const SegParams& p, int i, int* w) {
+__device__ __forceinline__ void decode_task(const SegParams& p, int nseg, const int4* segs, int* w) {
   w[0] = w[1] = w[2] = 0;
   w[3] = TASK_BAD;
-  const int4 h = load_header(p, i);
-  const int first = h.x, nseg = h.y;
-  if (nseg < 1 || nseg > kSegMax || first < 0 || int64_t(first) + nseg > p.num_kn_segs) return;
+  if (nseg < 1 || nseg > kSegMax) return;
   const int G = p.group;
-  const int4* segs = reinterpret_cast<const int4*>(p.kn_segs) + 2 * int64_t(first);
   int rows = 0, slot_end = 0, bad = 0, any = 0;
   for (int s = 0; s < nseg; ++s) {
-    const int4 a = segs[2 * s], b = segs[2 * s + 1];
+    const int4 a = segs[3 * s], b = segs[3 * s + 1], c = segs[3 * s + 2];
     int* sw = w + 4 + s * kSegWords;
     const int head = a.x, row0 = a.y, srows = a.z, slot = a.w, k0 = b.x, kt = b.y, kmax = b.z;
     const int job = b.w & 0x3fffffff, growing = (b.w >> 30) & 1;
@@ -159,6 +163,7 @@ __device__ __noinline__ void decode_task(const SegParams& p, int i, int* w) {
     sw[F_JOB] = job;
     sw[F_K0] = k0;
     sw[F_PROW0] = slot * G;
+    sw[F_Q0] = (c.x >= 0 && int64_t(c.x) + srows / G <= p.num_requests) ? c.x : -1;
     rows += srows;
     slot_end = kt + span;
     any |= nk;
@@ -239,12 +244,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = bars + S;
   uint64_t* v_full = bars + 2 * S;
   uint64_t* v_empty = bars + 3 * S;
-  uint64_t* s_full = bars + 4 * S;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* q_full = s_full + 4;
-  uint64_t* pv_done = s_full + 6;   // [2], by tile parity
-  uint64_t* q_empty = s_full + 8;   // [2], by Q^T buffer
-  uint64_t* task_full = s_full + 10;
+  uint64_t* s_full = bars + 4 * S;            // [kLook], by tile index mod kLook
+  uint64_t* p_full = s_full + kLook;
+  uint64_t* pv_done = p_full + kLook;
+  constexpr int QB = C::kQBufs;
+  uint64_t* q_full = pv_done + kLook;        // [QB], by Q^T buffer
+  uint64_t* q_empty = q_full + QB;
+  uint64_t* task_full = q_empty + QB;
   uint64_t* task_empty = task_full + kTQ;
   int* tasks = reinterpret_cast<int*>(smem + C::off_tasks);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::off_tmem);
@@ -266,11 +272,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kLook; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 4);
-      mbar_init(&q_full[b], 1);
       mbar_init(&pv_done[b], 1);
+    }
+    for (int b = 0; b < QB; ++b) {
+      mbar_init(&q_full[b], 1);
       mbar_init(&q_empty[b], 1);
     }
     for (int b = 0; b < kTQ; ++b) {
@@ -294,43 +302,77 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* qbuf = smem + C::off_q;
     int qi = 0;
     bool alive = true;
+    // Software pipeline over the list: while task k is decoded and its Q^T
+    // gathered, the segment records of task k+1 (whose header arrived during
+    // task k-1) and the header of task k+2 are in flight.
+    int4* stage = reinterpret_cast<int4*>(smem + C::off_stage);     // [2][3 * kSegMax]
+    auto header_ok = [&](int4 h) { return h.y >= 1 && h.y <= kSegMax && h.x >= 0 && int64_t(h.x) + h.y <= p.num_kn_segs; };
+    int4 hdr = count > 0 ? load_header(p, begin) : make_int4(0, 0, 0, 0);
+    if (count > 0 && header_ok(hdr) && lane < 3 * hdr.y)
+      stage[lane] = reinterpret_cast<const int4*>(p.kn_segs)[3 * int64_t(hdr.x) + lane];
+    int4 hdr_next = count > 1 ? load_header(p, begin + 1) : make_int4(0, 0, 0, 0);
+    __syncwarp();
     for (int k = 0; k < count && alive; ++k) {
       int* w = slot_of(k);
+      // prefetch: records of task k+1, header of task k+2
+      int4 pre = make_int4(0, 0, 0, 0);
+      const bool pre_ok = k + 1 < count && header_ok(hdr_next) && lane < 3 * hdr_next.y;
+      if (pre_ok) pre = reinterpret_cast<const int4*>(p.kn_segs)[3 * int64_t(hdr_next.x) + lane];
+      const int4 hdr_after = k + 2 < count ? load_header(p, begin + k + 2) : make_int4(0, 0, 0, 0);
       if (k >= kTQ) {
         int ok = 1;
         if (lane == 0) ok = mbar_wait(&task_empty[k % kTQ], ((k / kTQ) - 1) & 1, p.status);
         if (!__shfl_sync(0xffffffffu, ok, 0)) { alive = false; break; }
       }
       if (lane == 0) {
-        decode_task<R>(p, begin + k, w);
+        decode_task<R>(p, header_ok(hdr) ? hdr.y : 0, stage + (k & 1) * 3 * kSegMax, w);
         mbar_arrive(&task_full[k % kTQ]);
       }
       __syncwarp();
+      if (pre_ok) stage[((k + 1) & 1) * 3 * kSegMax + lane] = pre;
+      hdr = hdr_next;
+      hdr_next = hdr_after;
+      __syncwarp();
       if (w[0] == 0 || w[1] == 0) continue;          // no tiles: no Q^T
-      const int qb = qi & 1;
-      if (qi >= 2) {
+      const int qb = qi % QB;
+      if (qi >= QB) {
         int ok = 1;
-        if (lane == 0) ok = mbar_wait(&q_empty[qb], ((qi >> 1) - 1) & 1, p.status);
+        if (lane == 0) ok = mbar_wait(&q_empty[qb], ((qi / QB) - 1) & 1, p.status);
         if (!__shfl_sync(0xffffffffu, ok, 0)) { alive = false; break; }
       }
-      // rows x 16 chunks of 16 bytes, swizzled K-major
-      unsigned char* dst = qbuf + qb * C::kQBytes;
+      // rows x 16 chunks of 16 bytes, swizzled K-major: loads first, stores after
       const int rows = w[2];
-      for (int e = lane; e < rows * 16; e += 32) {
-        const int r = e >> 4, c = e & 15;
-        int s = 0;
+      unsigned char* dst = qbuf + qb * C::kQBytes;
+      for (int e0 = 0; e0 < rows * 16; e0 += 4 * 32) {
+        uint4 v[4];
 #pragma unroll
-        for (int x = 1; x < kSegMax; ++x)
-          if (x < w[0] && r >= w[4 + x * kSegWords + F_ROW0]) s = x;
-        const int* sw = w + 4 + s * kSegWords;
-        const int lr = r - sw[F_ROW0];
-        const int rid = p.qids[int64_t(sw[F_JOB]) * p.max_requests + lr / G];
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (rid >= 0 && rid < p.num_requests)
-          v = *reinterpret_cast<const uint4*>(p.q + (int64_t(rid) * p.num_q_heads + sw[F_HEAD] * G + lr % G) * kDim + c * 8);
-        else
-          set_status(p.status, TA_ERR_BOUNDS);
-        *reinterpret_cast<uint4*>(dst + (c >> 3) * C::kQHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+        for (int u = 0; u < 4; ++u) {
+          const int e = e0 + u * 32 + lane;
+          v[u] = make_uint4(0, 0, 0, 0);
+          if (e < rows * 16) {
+            const int r = e >> 4;
+            int s = 0;
+#pragma unroll
+            for (int x = 1; x < kSegMax; ++x)
+              if (x < w[0] && r >= w[4 + x * kSegWords + F_ROW0]) s = x;
+            const int* sw = w + 4 + s * kSegWords;
+            const int lr = r - sw[F_ROW0];
+            const int rid = sw[F_Q0] >= 0 ? sw[F_Q0] + lr / G : p.qids[int64_t(sw[F_JOB]) * p.max_requests + lr / G];
+            if (rid >= 0 && rid < p.num_requests)
+              v[u] = *reinterpret_cast<const uint4*>(p.q + (int64_t(rid) * p.num_q_heads + sw[F_HEAD] * G + lr % G) * kDim +
+                                                      (e & 15) * 8);
+            else
+              set_status(p.status, TA_ERR_BOUNDS);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = e0 + u * 32 + lane;
+          if (e < rows * 16) {
+            const int r = e >> 4, c = e & 15;
+            *reinterpret_cast<uint4*>(dst + (c >> 3) * C::kQHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v[u];
+          }
+        }
       }
       fence_async_smem();
       __syncwarp();
@@ -393,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pdesc0 = smem_desc(smem_u32(smem + C::off_p), 16, 1024);
       bool alive = true;
 
-      // Two cursors over the CTA's tiles: `sc` issues S two tiles ahead of `pc`.
+      // Two cursors over the CTA's tiles: `sc` issues S kLook tiles ahead of `pc`.
       // Tasks without tiles are skipped; `qi` counts the tasks with tiles,
       // which alone use the Q^T and O^T buffers.  The S cursor waits for each
       // task slot; the P.V cursor, which trails it, releases every slot.
@@ -426,28 +468,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto issue_s = [&](const Cursor& c) -> bool {
         const int st = c.g % S;
-        if (c.j == 0 && !mbar_wait(&q_full[c.qi & 1], (c.qi >> 1) & 1, p.status)) return false;
+        if (c.j == 0 && !mbar_wait(&q_full[c.qi % QB], (c.qi / QB) & 1, p.status)) return false;
         if (!mbar_wait(&k_full[st], (c.g / S) & 1, p.status)) return false;
         tc_fence_after();
         const uint64_t kd = kdesc0 + ((uint64_t(st) * kTileBytes) >> 4);
-        const uint64_t qd = qdesc0 + ((uint64_t(c.qi & 1) * C::kQBytes) >> 4);
-        const uint32_t d = tmem + uint32_t(c.g & 1) * N;
+        const uint64_t qd = qdesc0 + ((uint64_t(c.qi % QB) * C::kQBytes) >> 4);
+        const uint32_t d = tmem + uint32_t(c.g % kLook) * N;
 #pragma unroll
         for (int s = 0; s < kDim / 16; ++s) {
           const uint64_t ka = ((s >> 2) * kHalfBytes + (s & 3) * 32) >> 4;
           const uint64_t qa = ((s >> 2) * C::kQHalf + (s & 3) * 32) >> 4;
           umma_ss(d, kd + ka, qd + qa, idesc_s, s > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[c.g & 1]);
+        umma_commit(&s_full[c.g % kLook]);
         umma_commit(&k_empty[st]);
-        if (c.j == c.w[1] - 1) umma_commit(&q_empty[c.qi & 1]);    // the task's last S: its Q^T buffer is free
+        if (c.j == c.w[1] - 1) umma_commit(&q_empty[c.qi % QB]);   // the task's last S: its Q^T buffer is free
         return true;
       };
       // P.V reads key rows [0, 16 * steps); every such row that is not a live
       // key of its slot is zeroed first.
       auto issue_pv = [&](const Cursor& c) -> bool {
         const int st = c.g % S;
-        if (!mbar_wait(&p_full[c.g & 1], (c.g >> 1) & 1, p.status)) return false;
+        if (!mbar_wait(&p_full[c.g % kLook], (c.g / kLook) & 1, p.status)) return false;
         if (!mbar_wait(&v_full[st], (c.g / S) & 1, p.status)) return false;
         const int* w = c.w;
         const int nseg = w[0];
@@ -477,8 +519,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint64_t vd = vdesc0 + ((uint64_t(st) * kTileBytes) >> 4);
-        const uint64_t pd = pdesc0 + ((uint64_t(c.g & 1) * C::kQBytes) >> 4);
-        const uint32_t o = tmem + 2 * N + uint32_t(c.qi & 1) * N;     // O^T of this task's parity
+        const uint64_t pd = pdesc0 + ((uint64_t(c.g % kLook) * C::kQBytes) >> 4);
+        const uint32_t o = tmem + kLook * N + uint32_t(c.qi & 1) * N;     // O^T of this task's parity
 #pragma unroll 1
         for (int s = 0; s < steps; ++s) {
           const uint64_t va = (uint64_t(s) * 2048) >> 4;           // 16 keys = two 8-row atoms
@@ -486,19 +528,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_ss(o, vd + va, pd + pa, idesc_pv, (c.j > 0 || s > 0) ? 1u : 0u);
         }
         umma_commit(&v_empty[st]);
-        umma_commit(&pv_done[c.g & 1]);
+        umma_commit(&pv_done[c.g % kLook]);
         return true;
       };
 
       Cursor sc{0, 0, 0, 0, nullptr}, pc{0, 0, 0, 0, nullptr};
       settle(sc, true);
-      for (int k = 0; k < 2 && sc.k < count && alive; ++k) {
+      for (int k = 0; k < kLook && sc.k < count && alive; ++k) {
         alive = issue_s(sc);
         advance(sc, true);
       }
       if (alive) settle(pc, false);
-      // P.V(g) as soon as its inputs are in, then S(g+2).  P.V(g) must not wait
-      // for S(g+2)'s inputs: those depend on softmax progress that waits for P.V(g).
+      // P.V(g) as soon as its inputs are in, then S(g+3).  P.V(g) must not wait
+      // for S(g+3)'s inputs: those depend on softmax progress that waits for P.V(g).
       while (pc.k < count && alive) {
         alive = issue_pv(pc);
         if (!alive) break;
@@ -547,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // and row statistics sit in buffer `b`: O / l and the LSE of every row.
     auto epilogue = [&](int k, int g_last, int b) {
       const int* w = slot_of(k);
-      const bool w_ok = alive && warp_wait(&pv_done[g_last & 1], (g_last >> 1) & 1, p.status);
+      const bool w_ok = alive && warp_wait(&pv_done[g_last % kLook], (g_last / kLook) & 1, p.status);
       if (named_sync_or(2, kSoftmaxThreads, !w_ok)) alive = false;     // also orders suml / mfin
       const bool o_ok = alive;
       if (o_ok) tc_fence_after();
@@ -566,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint32_t o[CW];
           if (o_ok) {
-            tmem_ldw<CW>(lane_base + 2 * N + uint32_t(b) * N + c * CW, o);
+            tmem_ldw<CW>(lane_base + kLook * N + uint32_t(b) * N + c * CW, o);
             tmem_wait_ld();
           }
 #pragma unroll
@@ -617,7 +659,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       for (int j = 0; j < ntiles; ++j, ++g) {
-        const int b = g & 1;
+        const int b = g & 1;               // tile-maxima exchange buffer
+        const int sb = g % kLook;          // S^T / P^T buffer and its barriers
         // rows whose segment has this thread's key as a live key in this tile
         uint64_t live_rows = 0;
 #pragma unroll 1
@@ -626,8 +669,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int lo = sw[F_KT], keys = slot_keys(w, s, j);
           if (kk >= lo && kk < lo + keys) live_rows |= row_mask(sw[F_ROW0], sw[F_ROWS]);
         }
-        const bool ok = alive && warp_wait(&s_full[b], (g >> 1) & 1, p.status);
-        const uint32_t s_addr = lane_base + uint32_t(b) * N;
+        const bool ok = alive && warp_wait(&s_full[sb], (g / kLook) & 1, p.status);
+        const uint32_t s_addr = lane_base + uint32_t(sb) * N;
         uint32_t keep[CW];          // scores of the first (for R <= 16: the only) column group
         bool need = false;
         if (ok) {
@@ -688,12 +731,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           named_sync(2, kSoftmaxThreads);
           bool o_ok = j > 0;
           if (j > 0) {
-            const bool w_ok = warp_wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, p.status);
+            const bool w_ok = warp_wait(&pv_done[(g - 1) % kLook], ((g - 1) / kLook) & 1, p.status);
             if (named_sync_or(2, kSoftmaxThreads, !w_ok)) alive = false;
             o_ok = alive;
             if (o_ok) tc_fence_after();
           }
-          const uint32_t o_addr = lane_base + 2 * N + uint32_t(qi & 1) * N;
+          const uint32_t o_addr = lane_base + kLook * N + uint32_t(qi & 1) * N;
 #pragma unroll
           for (int c = 0; c < NC; ++c) {
             if (c * CW < rows) {
@@ -721,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // P^T = exp2(s - m) over each row's live keys, bf16/f16, K-major swizzled
         if (alive) {
-          unsigned char* pt = pbuf + b * C::kQBytes;
+          unsigned char* pt = pbuf + sb * C::kQBytes;
 #pragma unroll
           for (int c = 0; c < NC; ++c) {
             if (c * CW < rows) {
@@ -750,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[b]);
+        if (lane == 0) mbar_arrive(&p_full[sb]);
         if (j == 0 && pend_k >= 0) {
           // the previous task's epilogue: its P.V has had this tile to finish
           epilogue(pend_k, pend_g, (qi - 1) & 1);

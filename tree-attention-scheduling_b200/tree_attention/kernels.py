@@ -164,7 +164,7 @@ KN_PACK_SEGS = 4     # segments of a packed tile
 def pack_segments(items):
     """Group keys-in-lanes segments into tasks.
 
-    ``items`` are ``(head, rows, slot, k0, keys, job_flags)``.  A segment of more
+    ``items`` are ``(head, rows, slot, k0, keys, job_flags, first_request)``.  A segment of more
     than one 128-key tile is a task of its own; shorter ones are packed, best
     fit by their 32-key-rounded span, into tiles of 128 keys, at most
     KN_PACK_SEGS segments and KN_PACK_ROWS query rows each (a segment of more
@@ -281,8 +281,11 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
     for p, (i, offset, take) in enumerate(piece_list):
         if route[i] == "kn":
             growing = int(no_split_from is not None and jobs[i].tokens[0] >= no_split_from)
+            reqs = jobs[i].requests
+            q0 = reqs[0] if reqs[-1] - reqs[0] + 1 == len(reqs) else -1
             for h in range(heads):
-                items.append((h, rows[i], int(pieces[p, 3]), jobs[i].tokens[0] + offset, take, i | (growing << 30)))
+                items.append((h, rows[i], int(pieces[p, 3]), jobs[i].tokens[0] + offset, take, i | (growing << 30),
+                              q0))
         elif route[i] == "tc":
             tc.extend((p, t) for t in range(ceil(rows[i] / TC_ROWS)))
         else:
@@ -300,8 +303,8 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
     for task in tasks:
         headers.append((len(segs), len(task), 0, 0))
         row0, kt = 0, 0
-        for h, r, first_slot, k0, keys, job in task:
-            segs.append((h, row0, r, first_slot, k0, kt if len(task) > 1 else 0, keys, job))
+        for h, r, first_slot, k0, keys, job, q0 in task:
+            segs.append((h, row0, r, first_slot, k0, kt if len(task) > 1 else 0, keys, job, q0, 0, 0, 0))
             row0 += r
             kt += -(-keys // KN_BOX) * KN_BOX
         costs.append(_tiles(max(s[4] for s in task)) + 1)
@@ -311,7 +314,7 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
         kn_tasks = np.array(headers, dtype=np.int32)[order]
     else:
         kn_offsets, kn_tasks = np.zeros(1, dtype=np.int32), np.zeros((0, 4), dtype=np.int32)
-    kn_segs = np.array(segs, dtype=np.int32).reshape(-1, 8)
+    kn_segs = np.array(segs, dtype=np.int32).reshape(-1, 12)
     return dict(qids=qids, kids=kids, qlen=qlen, klen=klen, slots=slots, counts=counts,
                 pieces=pieces, pcounts=pcounts, cslots=cslots, small_tasks=small_tasks, tc_tasks=tc_tasks,
                 kn_offsets=kn_offsets, kn_tasks=kn_tasks, kn_segs=kn_segs, small_class_end=class_end,
