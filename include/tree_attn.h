@@ -42,7 +42,7 @@
  *                                           keys-in-lanes tcgen05 kernel
  *   kn_tasks    [num_kn_tasks, 4]           its task headers: first segment, segments, 0, 0
  *   kn_segs     [num_kn_segs, 12]           segments: KV head, first query row in the
- *                                           task, query rows, first partial slot, first
+ *                                           task, query rows, first partial row (slot * G), first
  *                                           pool position, first key of its slot in the
  *                                           tile, keys, job | growing << 30 (growing: keys
  *                                           = min(keys, klen[job]), a decode tail), first

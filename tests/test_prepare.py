@@ -75,9 +75,10 @@ def check_b200_arrays(p, groups, heads=None):
     for first, nseg, _, _ in meta["kn_tasks"]:
         assert 1 <= nseg <= kernels.KN_PACK_SEGS
         row0 = kt = 0
-        for head, r0, rows, slot, k0, seg_kt, keys, jobf, q0, _, _, _ in segs[first:first + nseg]:
+        for head, r0, rows, prow, k0, seg_kt, keys, jobf, q0, _, _, _ in segs[first:first + nseg]:
             job, growing = int(jobf) & 0x3FFFFFFF, int(jobf) >> 30
-            pc = slot_piece[int(slot)]
+            assert prow % groups == 0
+            pc = slot_piece[int(prow) // groups]
             assert pieces[pc, 0] == job and keys == pieces[pc, 2] and rows == qlen[job] * groups
             assert k0 == p.jobs[job].tokens[0] + pieces[pc, 1] and growing in (0, 1)
             reqs = p.jobs[job].requests

@@ -99,6 +99,7 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
   p.num_kn_segs = plan->num_kn_segs;
   p.kn_ctas = plan->kn_ctas;
   p.scale_log2 = kLog2e / std::sqrt(float(head_dim));
+  p.gmul = (65536u + uint32_t(p.group) - 1u) / uint32_t(p.group);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err = cudaSuccess;

@@ -80,13 +80,51 @@ constexpr uint32_t kHalfBytes = kTileBytes / 2;            // one 64-column swiz
 constexpr uint32_t kBoxBytes = kBoxRows * 128;              // one 32-row x 64-column box
 constexpr float kRescaleThreshold = 8.0f;                   // log2 units
 constexpr int kLook = 3;                    // S runs this many tiles ahead of P.V (S / P buffers)
-// task slot words: nseg, ntiles, rows, flags, then per segment
-// head, row0, rows, keys now, first key of its slot, slot keys, job, k0, first
-// partial row, first request (-1 unless the job's requests are contiguous)
-constexpr int kSegWords = 10;
-constexpr int kTaskWords = 4 + kSegMax * kSegWords;         // 44
+// task slot: int4 {nseg, ntiles, rows, flags}, then per segment three int4
+// {head, row0, rows, keys now} {first key of its slot, slot keys, job, k0}
+// {first partial row, first request (-1 unless the job's requests are
+// contiguous), 0, 0}.  Every role copies a slot into registers with vector
+// loads once per task (no shared-memory store in between), so no access to it
+// waits on another.
+constexpr int kSegWords = 12;
+constexpr int kTaskWords = 4 + kSegMax * kSegWords;         // 52
 enum TaskFlag { TASK_BAD = 1, TASK_WRITE = 2 };
-enum SegField { F_HEAD, F_ROW0, F_ROWS, F_NK, F_KT, F_SPAN, F_JOB, F_K0, F_PROW0, F_Q0 };
+
+struct SegR {
+  int head, row0, rows, nk, kt, span, job, k0, prow0, q0;
+};
+struct TaskR {
+  int nseg, ntiles, rows, flags;
+  SegR seg[kSegMax];
+};
+
+__device__ __forceinline__ TaskR load_task(const int* w) {
+  const int4* v = reinterpret_cast<const int4*>(w);
+  const int4 h = v[0];
+  TaskR t;
+  t.nseg = h.x;
+  t.ntiles = h.y;
+  t.rows = h.z;
+  t.flags = h.w;
+#pragma unroll
+  for (int s = 0; s < kSegMax; ++s) {
+    const int4 a = v[1 + 3 * s], b = v[2 + 3 * s], c = v[3 + 3 * s];
+    t.seg[s] = SegR{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y};
+  }
+  return t;
+}
+
+__device__ __forceinline__ void store_task(int* w, const TaskR& t) {
+  int4* v = reinterpret_cast<int4*>(w);
+  v[0] = make_int4(t.nseg, t.ntiles, t.rows, t.flags);
+#pragma unroll
+  for (int s = 0; s < kSegMax; ++s) {
+    const SegR& g = t.seg[s];
+    v[1 + 3 * s] = make_int4(g.head, g.row0, g.rows, g.nk);
+    v[2 + 3 * s] = make_int4(g.kt, g.span, g.job, g.k0);
+    v[3 + 3 * s] = make_int4(g.prow0, g.q0, 0, 0);
+  }
+}
 
 template <int R>
 struct KnCfg {
@@ -106,7 +144,8 @@ struct KnCfg {
   static constexpr uint32_t off_mfin = off_suml + 2 * 4 * R * 4;      // [2][R] final row maxima, by task parity
   static constexpr uint32_t off_tasks = off_mfin + 2 * R * 4;         // [kTQ][kTaskWords] task slots
   static constexpr uint32_t off_stage = off_tasks + kTQ * kTaskWords * 4;   // [2][3 * kSegMax] int4 staged segment records
-  static constexpr uint32_t off_bar = off_stage + 2 * 3 * kSegMax * 16;
+  static constexpr uint32_t off_rowsrc = off_stage + 2 * 3 * kSegMax * 16;  // [R] int64 Q row offsets of a task
+  static constexpr uint32_t off_bar = off_rowsrc + R * 8;
   // k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[L], p_full[L], pv_done[L], q_full[QB],
   // q_empty[QB], task_full[kTQ], task_empty[kTQ]
   static constexpr int kBars = 4 * kStages + 3 * kLook + 2 * kQBufs + 2 * kTQ;
@@ -123,62 +162,69 @@ __device__ __forceinline__ int4 load_header(const SegParams& p, int i) {
   return reinterpret_cast<const int4*>(p.kn_tasks)[i];
 }
 
-// Decode and check one task into a task slot (one thread).  `nseg` and the
-// task's segment records, staged in shared memory, are as the host wrote them
-// (12 int32 each): KV head, first query row of the tile's N rows, rows, first
-// partial slot, first pool position, first key of its slot in the tile, keys
-// (at most), job | growing << 30, first request of the job if its requests
-// are contiguous (else -1), 0, 0, 0.
+// Decode and check one task into a task slot (the scheduler warp; lane s
+// checks segment s).  `nseg` and the task's segment records, staged in shared
+// memory, are as the host wrote them (12 int32 each): KV head, first query row
+// of the tile's N rows, rows, first partial row (slot * G), first pool
+// position, first key of its slot in the tile, keys (at most), job | growing
+// << 30, first request of the job if its requests are contiguous (else -1),
+// 0, 0, 0.  Segment s must start where segment s-1 ends, in rows and in tile
+// keys; a task with any malformed segment gets nseg 0 and writes nothing.
 template <int R>
-__device__ __forceinline__ void decode_task(const SegParams& p, int nseg, const int4* segs, int* w) {
-  w[0] = w[1] = w[2] = 0;
-  w[3] = TASK_BAD;
-  if (nseg < 1 || nseg > kSegMax) return;
+__device__ __forceinline__ void decode_task(const SegParams& p, int nseg, const int4* segs, int* w, int lane) {
   const int G = p.group;
-  int rows = 0, slot_end = 0, bad = 0, any = 0;
-  for (int s = 0; s < nseg; ++s) {
-    const int4 a = segs[3 * s], b = segs[3 * s + 1], c = segs[3 * s + 2];
-    int* sw = w + 4 + s * kSegWords;
-    const int head = a.x, row0 = a.y, srows = a.z, slot = a.w, k0 = b.x, kt = b.y, kmax = b.z;
-    const int job = b.w & 0x3fffffff, growing = (b.w >> 30) & 1;
-    const int span = ((kmax + kBoxRows - 1) / kBoxRows) * kBoxRows;
-    if (head < 0 || head >= p.num_kv_heads || job < 0 || job >= p.num_jobs || srows < 1 || srows % G ||
-        srows / G > p.max_requests || row0 != rows || slot < 0 || int64_t(slot) + srows / G > p.num_partials ||
-        kmax < 0 || kt != slot_end || (nseg > 1 && kt + span > kKeys) ||
-        int64_t(p.num_partials) * G > INT32_MAX)
-      return;                                      // nothing of this task may be written
-    int nk = kmax;
-    if (growing) nk = min(kmax, p.klen[job]);      // a growing decode tail (always a whole job)
-    if (nk < 0) nk = 0;
-    if (k0 < 0 || int64_t(k0) + nk > p.pool_tokens || k0 > INT32_MAX - 512) {
-      nk = 0;
-      bad = 1;
-    }
-    sw[F_HEAD] = head;
-    sw[F_ROW0] = row0;
-    sw[F_ROWS] = srows;
-    sw[F_NK] = nk;
-    sw[F_KT] = kt;
-    sw[F_SPAN] = nseg == 1 ? kKeys : span;
-    sw[F_JOB] = job;
-    sw[F_K0] = k0;
-    sw[F_PROW0] = slot * G;
-    sw[F_Q0] = (c.x >= 0 && int64_t(c.x) + srows / G <= p.num_requests) ? c.x : -1;
-    rows += srows;
-    slot_end = kt + span;
-    any |= nk;
+  const bool mine = lane < kSegMax && lane < nseg;
+  int4 a = make_int4(0, 0, 0, 0), b = a, c = a;
+  if (mine) {
+    a = segs[3 * lane];
+    b = segs[3 * lane + 1];
+    c = segs[3 * lane + 2];
   }
-  if (rows > R) return;
-  w[0] = nseg;
-  w[1] = nseg == 1 ? (w[4 + F_NK] + kKeys - 1) / kKeys : (any ? 1 : 0);
-  w[2] = rows;
-  w[3] = TASK_WRITE | (bad ? TASK_BAD : 0);
+  const int head = a.x, row0 = a.y, srows = a.z, prow0 = a.w, k0 = b.x, kt = b.y, kmax = b.z;
+  const int job = b.w & 0x3fffffff, growing = (b.w >> 30) & 1;
+  const bool rows_ok = srows >= 1 && srows <= R;
+  const int nreq = rows_ok ? int((uint32_t(srows) * p.gmul) >> 16) : 0;   // srows / G (srows <= 64, G <= 64)
+  const bool kmax_ok = kmax >= 0 && kmax <= INT32_MAX - 512;
+  const int span = kmax_ok ? ((kmax + kBoxRows - 1) / kBoxRows) * kBoxRows : 0;
+  bool ok = rows_ok && kmax_ok && nreq * G == srows && nreq <= p.max_requests && head >= 0 &&
+            head < p.num_kv_heads && job >= 0 && job < p.num_jobs && prow0 >= 0 &&
+            int64_t(prow0) + srows <= int64_t(p.num_partials) * G && (nseg == 1 || kt + span <= kKeys);
+  // chain: this segment starts where the previous one ends
+  const int rend = __shfl_up_sync(0xffffffffu, row0 + srows, 1);
+  const int kend = __shfl_up_sync(0xffffffffu, kt + span, 1);
+  ok = ok && (lane == 0 ? (row0 == 0 && kt == 0) : (row0 == rend && kt == kend));
+  int nk = kmax;
+  if (mine && growing) nk = min(kmax, p.klen[job]);   // a growing decode tail (always a whole job)
+  if (nk < 0) nk = 0;
+  bool bad = false;
+  if (k0 < 0 || int64_t(k0) + nk > p.pool_tokens || k0 > INT32_MAX - 512) {
+    nk = 0;
+    bad = true;
+  }
+  const int q0 = (c.x >= 0 && int64_t(c.x) + nreq <= p.num_requests) ? c.x : -1;
+  const bool all_ok = nseg >= 1 && nseg <= kSegMax && __all_sync(0xffffffffu, !mine || ok);
+  const int rows = __shfl_sync(0xffffffffu, row0 + srows, (nseg - 1) & 31);
+  const bool any = __any_sync(0xffffffffu, mine && nk > 0);
+  const bool any_bad = __any_sync(0xffffffffu, mine && bad);
+  const int nk0 = __shfl_sync(0xffffffffu, nk, 0);
+  const bool good = all_ok && rows <= R;
+  int4* v = reinterpret_cast<int4*>(w);
+  if (lane < kSegMax) {
+    const bool keep = good && mine;
+    v[1 + 3 * lane] = keep ? make_int4(head, row0, srows, nk) : make_int4(0, 0, 0, 0);
+    v[2 + 3 * lane] = keep ? make_int4(kt, nseg == 1 ? kKeys : span, job, k0) : make_int4(0, 0, 0, 0);
+    v[3 + 3 * lane] = keep ? make_int4(prow0, q0, 0, 0) : make_int4(0, -1, 0, 0);
+  }
+  if (lane == 0) {
+    v[0] = good ? make_int4(nseg, nseg == 1 ? (nk0 + kKeys - 1) / kKeys : (any ? 1 : 0), rows,
+                            TASK_WRITE | (any_bad ? TASK_BAD : 0))
+                : make_int4(0, 0, 0, TASK_BAD);
+  }
 }
 
-// Keys of segment s of a task slot inside tile j (a packed task has one tile).
-__device__ __forceinline__ int slot_keys(const int* w, int s, int j) {
-  const int nk = w[4 + s * kSegWords + F_NK];
-  return w[0] == 1 ? min(kKeys, nk - j * kKeys) : nk;
+// Keys of segment s inside tile j (a packed task has one tile).
+__device__ __forceinline__ int seg_keys(const TaskR& t, int s, int j) {
+  return t.nseg == 1 ? min(kKeys, t.seg[0].nk - j * kKeys) : t.seg[s].nk;
 }
 
 __device__ __forceinline__ uint64_t row_mask(int row0, int rows) {
@@ -306,6 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // gathered, the segment records of task k+1 (whose header arrived during
     // task k-1) and the header of task k+2 are in flight.
     int4* stage = reinterpret_cast<int4*>(smem + C::off_stage);     // [2][3 * kSegMax]
+    int64_t* rowsrc = reinterpret_cast<int64_t*>(smem + C::off_rowsrc);
     auto header_ok = [&](int4 h) { return h.y >= 1 && h.y <= kSegMax && h.x >= 0 && int64_t(h.x) + h.y <= p.num_kn_segs; };
     int4 hdr = count > 0 ? load_header(p, begin) : make_int4(0, 0, 0, 0);
     if (count > 0 && header_ok(hdr) && lane < 3 * hdr.y)
@@ -324,24 +371,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) ok = mbar_wait(&task_empty[k % kTQ], ((k / kTQ) - 1) & 1, p.status);
         if (!__shfl_sync(0xffffffffu, ok, 0)) { alive = false; break; }
       }
-      if (lane == 0) {
-        decode_task<R>(p, header_ok(hdr) ? hdr.y : 0, stage + (k & 1) * 3 * kSegMax, w);
-        mbar_arrive(&task_full[k % kTQ]);
-      }
+      decode_task<R>(p, header_ok(hdr) ? hdr.y : 0, stage + (k & 1) * 3 * kSegMax, w, lane);
       __syncwarp();
+      if (lane == 0) mbar_arrive(&task_full[k % kTQ]);
       if (pre_ok) stage[((k + 1) & 1) * 3 * kSegMax + lane] = pre;
       hdr = hdr_next;
       hdr_next = hdr_after;
       __syncwarp();
-      if (w[0] == 0 || w[1] == 0) continue;          // no tiles: no Q^T
+      const TaskR t = load_task(w);
+      if (t.nseg == 0 || t.ntiles == 0) continue;    // no tiles: no Q^T
       const int qb = qi % QB;
       if (qi >= QB) {
         int ok = 1;
         if (lane == 0) ok = mbar_wait(&q_empty[qb], ((qi / QB) - 1) & 1, p.status);
         if (!__shfl_sync(0xffffffffu, ok, 0)) { alive = false; break; }
       }
-      // rows x 16 chunks of 16 bytes, swizzled K-major: loads first, stores after
-      const int rows = w[2];
+      // Each lane finds the Q row behind tile rows lane and lane + 32, then the
+      // warp copies rows x 16 chunks of 16 bytes, swizzled K-major: loads
+      // first, stores after.
+      const int rows = t.rows;
+      for (int r = lane; r < rows; r += 32) {
+        SegR sg = t.seg[0];
+#pragma unroll
+        for (int x = 1; x < kSegMax; ++x)
+          if (x < t.nseg && r >= t.seg[x].row0) sg = t.seg[x];
+        const int lr = r - sg.row0;
+        const int req = int((uint32_t(lr) * p.gmul) >> 16);         // lr / G (lr < 64, G <= 64)
+        const int rid = sg.q0 >= 0 ? sg.q0 + req : p.qids[int64_t(sg.job) * p.max_requests + req];
+        int64_t src_row = -1;
+        if (rid >= 0 && rid < p.num_requests)
+          src_row = (int64_t(rid) * p.num_q_heads + sg.head * G + (lr - req * G)) * kDim;
+        else
+          set_status(p.status, TA_ERR_BOUNDS);
+        rowsrc[r] = src_row;
+      }
+      __syncwarp();
       unsigned char* dst = qbuf + qb * C::kQBytes;
       for (int e0 = 0; e0 < rows * 16; e0 += 4 * 32) {
         uint4 v[4];
@@ -350,19 +414,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int e = e0 + u * 32 + lane;
           v[u] = make_uint4(0, 0, 0, 0);
           if (e < rows * 16) {
-            const int r = e >> 4;
-            int s = 0;
-#pragma unroll
-            for (int x = 1; x < kSegMax; ++x)
-              if (x < w[0] && r >= w[4 + x * kSegWords + F_ROW0]) s = x;
-            const int* sw = w + 4 + s * kSegWords;
-            const int lr = r - sw[F_ROW0];
-            const int rid = sw[F_Q0] >= 0 ? sw[F_Q0] + lr / G : p.qids[int64_t(sw[F_JOB]) * p.max_requests + lr / G];
-            if (rid >= 0 && rid < p.num_requests)
-              v[u] = *reinterpret_cast<const uint4*>(p.q + (int64_t(rid) * p.num_q_heads + sw[F_HEAD] * G + lr % G) * kDim +
-                                                      (e & 15) * 8);
-            else
-              set_status(p.status, TA_ERR_BOUNDS);
+            const int64_t s = rowsrc[e >> 4];
+            if (s >= 0) v[u] = *reinterpret_cast<const uint4*>(p.q + s + (e & 15) * 8);
           }
         }
 #pragma unroll
@@ -391,32 +444,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool alive = true;
       for (int k = 0; k < count && alive; ++k) {
         if (!mbar_wait(&task_full[k % kTQ], (k / kTQ) & 1, p.status)) break;
-        const int* w = slot_of(k);
-        const int nseg = w[0], ntiles = w[1];
-        for (int j = 0; j < ntiles; ++j, ++g) {
+        const TaskR t = load_task(slot_of(k));
+        mbar_arrive(&task_empty[k % kTQ]);           // the task now lives in registers
+        for (int j = 0; j < t.ntiles; ++j, ++g) {
           const int st = g % S;
           if (g >= S && !mbar_wait(&empty[st], ((g / S) + 1) & 1, p.status)) { alive = false; break; }
           int boxes_total = 0;
-#pragma unroll 1
-          for (int s = 0; s < nseg; ++s) boxes_total += (max(0, slot_keys(w, s, j)) + kBoxRows - 1) / kBoxRows;
+#pragma unroll
+          for (int s = 0; s < kSegMax; ++s)
+            if (s < t.nseg) boxes_total += (max(0, seg_keys(t, s, j)) + kBoxRows - 1) / kBoxRows;
           mbar_arrive_expect_tx(&full[st], uint32_t(boxes_total) * 2 * kBoxBytes);
           unsigned char* dst = ring + st * kTileBytes;
-          // (loops kept rolled: unrolled copies of the TMA issue made the
-          // kernel outgrow the instruction cache)
-#pragma unroll 1
-          for (int s = 0; s < nseg; ++s) {
-            const int* sw = w + 4 + s * kSegWords;
-            const int keys = max(0, slot_keys(w, s, j));
-            const int y = sw[F_K0] + j * kKeys;
+#pragma unroll
+          for (int s = 0; s < kSegMax; ++s) {
+            if (s >= t.nseg) break;
+            const SegR& sg = t.seg[s];
+            const int keys = max(0, seg_keys(t, s, j));
+            const int y = sg.k0 + j * kKeys;
+            // (kept rolled: unrolled copies of the TMA issue made the kernel
+            // outgrow the instruction cache)
 #pragma unroll 1
             for (int b = 0; b * kBoxRows < keys; ++b) {
-              const uint32_t row = uint32_t(sw[F_KT] + b * kBoxRows) * 128u;
-              tma_load_3d(dst + row, map, 0, y + b * kBoxRows, sw[F_HEAD], &full[st]);
-              tma_load_3d(dst + kHalfBytes + row, map, 64, y + b * kBoxRows, sw[F_HEAD], &full[st]);
+              const uint32_t row = uint32_t(sg.kt + b * kBoxRows) * 128u;
+              tma_load_3d(dst + row, map, 0, y + b * kBoxRows, sg.head, &full[st]);
+              tma_load_3d(dst + kHalfBytes + row, map, 64, y + b * kBoxRows, sg.head, &full[st]);
             }
           }
         }
-        mbar_arrive(&task_empty[k % kTQ]);
       }
       // Nothing may still be landing when the CTA exits: wait (bounded) for
       // the last loads of each ring slot.
@@ -441,8 +495,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // task slot; the P.V cursor, which trails it, releases every slot.
       struct Cursor {
         int k, j, g, qi;      // index within the list, tile in task, global tile, index among tasks with tiles
-        const int* w;
+        TaskR t;
       };
+      // The lead (S) cursor waits for each task slot; the trailing (P.V)
+      // cursor copies it to registers and releases it for the MMA warp.
       auto settle = [&](Cursor& c, bool lead) {   // move to the next task with tiles
         while (c.k < count) {
           if (lead && !mbar_wait(&task_full[c.k % kTQ], (c.k / kTQ) & 1, p.status)) {
@@ -450,16 +506,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             c.k = count;
             return;
           }
-          c.w = slot_of(c.k);
-          if (c.w[0] > 0 && c.w[1] > 0) return;
+          c.t = load_task(slot_of(c.k));
           if (!lead) mbar_arrive(&task_empty[c.k % kTQ]);
+          if (c.t.nseg > 0 && c.t.ntiles > 0) return;
           ++c.k;
         }
       };
       auto advance = [&](Cursor& c, bool lead) {
         ++c.g;
-        if (++c.j >= c.w[1]) {
-          if (!lead) mbar_arrive(&task_empty[c.k % kTQ]);
+        if (++c.j >= c.t.ntiles) {
           c.j = 0;
           ++c.k;
           ++c.qi;
@@ -482,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&s_full[c.g % kLook]);
         umma_commit(&k_empty[st]);
-        if (c.j == c.w[1] - 1) umma_commit(&q_empty[c.qi % QB]);   // the task's last S: its Q^T buffer is free
+        if (c.j == c.t.ntiles - 1) umma_commit(&q_empty[c.qi % QB]);   // the task's last S: its Q^T buffer is free
         return true;
       };
       // P.V reads key rows [0, 16 * steps); every such row that is not a live
@@ -491,22 +546,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = c.g % S;
         if (!mbar_wait(&p_full[c.g % kLook], (c.g / kLook) & 1, p.status)) return false;
         if (!mbar_wait(&v_full[st], (c.g / S) & 1, p.status)) return false;
-        const int* w = c.w;
-        const int nseg = w[0];
+        const TaskR& t = c.t;
         int steps = 8;
-        if (nseg > 1 || slot_keys(w, 0, c.j) < kKeys) {
+        if (t.nseg > 1 || seg_keys(t, 0, c.j) < kKeys) {
           unsigned char* vt = smem + C::off_v + st * kTileBytes;
           int extent = 0;
-#pragma unroll 1
-          for (int s = 0; s < nseg; ++s)
-            if (slot_keys(w, s, c.j) > 0) extent = w[4 + s * kSegWords + F_KT] + slot_keys(w, s, c.j);
+#pragma unroll
+          for (int s = 0; s < kSegMax; ++s)
+            if (s < t.nseg && seg_keys(t, s, c.j) > 0) extent = t.seg[s].kt + seg_keys(t, s, c.j);
           steps = (extent + 15) >> 4;
           bool zeroed = false;
-#pragma unroll 1
-          for (int s = 0; s < nseg; ++s) {
-            const int kt = w[4 + s * kSegWords + F_KT];
-            const int lo = kt + max(0, slot_keys(w, s, c.j));
-            const int hi = min(kt + w[4 + s * kSegWords + F_SPAN], 16 * steps);
+#pragma unroll
+          for (int s = 0; s < kSegMax; ++s) {
+            if (s >= t.nseg) break;
+            const int kt = t.seg[s].kt;
+            const int lo = kt + max(0, seg_keys(t, s, c.j));
+            const int hi = min(kt + t.seg[s].span, 16 * steps);
 #pragma unroll 1
             for (int r = lo; r < hi; ++r) {
 #pragma unroll
@@ -532,7 +587,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
 
-      Cursor sc{0, 0, 0, 0, nullptr}, pc{0, 0, 0, 0, nullptr};
+      Cursor sc, pc;
+      sc.k = sc.j = sc.g = sc.qi = 0;
+      pc.k = pc.j = pc.g = pc.qi = 0;
       settle(sc, true);
       for (int k = 0; k < kLook && sc.k < count && alive; ++k) {
         alive = issue_s(sc);
@@ -573,13 +630,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool alive = true;
 
     // Partial row of task row r (rows are laid out segment after segment).
-    auto out_row = [&](const int* w, int r) -> int64_t {
-      int s = 0;
+    auto out_row = [&](const TaskR& t, int r) -> int64_t {
+      SegR sg = t.seg[0];
 #pragma unroll
       for (int x = 1; x < kSegMax; ++x)
-        if (x < w[0] && r >= w[4 + x * kSegWords + F_ROW0]) s = x;
-      const int* sw = w + 4 + s * kSegWords;
-      return int64_t(sw[F_HEAD]) * head_stride + sw[F_PROW0] + (r - sw[F_ROW0]);
+        if (x < t.nseg && r >= t.seg[x].row0) sg = t.seg[x];
+      return int64_t(sg.head) * head_stride + sg.prow0 + (r - sg.row0);
     };
     auto release = [&](int k) {
       __syncwarp();
@@ -588,14 +644,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Epilogue of a task with tiles whose last tile was `g_last` and whose O^T
     // and row statistics sit in buffer `b`: O / l and the LSE of every row.
     auto epilogue = [&](int k, int g_last, int b) {
-      const int* w = slot_of(k);
+      const TaskR t = load_task(slot_of(k));
       const bool w_ok = alive && warp_wait(&pv_done[g_last % kLook], (g_last / kLook) & 1, p.status);
       if (named_sync_or(2, kSoftmaxThreads, !w_ok)) alive = false;     // also orders suml / mfin
       const bool o_ok = alive;
       if (o_ok) tc_fence_after();
       const float* sl = suml + b * 4 * R;
       const float* mf = mfin + b * R;
-      const int rows = w[2];
+      const int rows = t.rows;
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
         if (c * CW < rows) {
@@ -615,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int q = 0; q < CW; ++q) {
             const int r = c * CW + q;
             if (r < rows) {
-              const int64_t row = out_row(w, r);
+              const int64_t row = out_row(t, r);
               const bool live = o_ok && z[q] > 0.f;
               p.part[row * kDim + kk] = live ? __uint_as_float(o[q]) * (1.f / z[q]) : 0.f;
               if (kk == r) p.lse[row] = live ? (mr[q] + fast_log2(z[q])) * kLn2 : -INFINITY;
@@ -634,8 +690,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool t_ok = alive && warp_wait(&task_full[k % kTQ], (k / kTQ) & 1, p.status);
       if (named_sync_or(1, kSoftmaxThreads, !t_ok)) alive = false;
       if (!alive) break;
-      const int* w = slot_of(k);
-      const int nseg = w[0], ntiles = w[1], rows = w[2], flags = w[3];
+      const TaskR t = load_task(slot_of(k));
+      const int ntiles = t.ntiles, rows = t.rows, flags = t.flags;
       if ((flags & TASK_BAD) && kk == 0) set_status(p.status, TA_ERR_BOUNDS);
       if (!(flags & TASK_WRITE)) {
         release(k);
@@ -644,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ntiles == 0) {
         // an empty task: O = 0, LSE = -inf, no tensor work
         for (int r = 0; r < rows; ++r) {
-          const int64_t row = out_row(w, r);
+          const int64_t row = out_row(t, r);
           p.part[row * kDim + kk] = 0.f;
           if (kk == r) p.lse[row] = -INFINITY;
         }
@@ -657,18 +713,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         l[r] = 0.f;
         m[r] = -INFINITY;
       }
+      // Rows that see this thread's key: a packed task has one tile with a
+      // fixed set; a long segment's key is live while it is below the keys left.
+      const bool single = t.nseg == 1;
+      const int keys_total = t.seg[0].nk;
+      const uint64_t single_mask = row_mask(0, rows);
+      uint64_t packed_rows = 0;
+#pragma unroll
+      for (int s = 0; s < kSegMax; ++s)
+        if (s < t.nseg && kk >= t.seg[s].kt && kk < t.seg[s].kt + t.seg[s].nk)
+          packed_rows |= row_mask(t.seg[s].row0, t.seg[s].rows);
 
       for (int j = 0; j < ntiles; ++j, ++g) {
         const int b = g & 1;               // tile-maxima exchange buffer
         const int sb = g % kLook;          // S^T / P^T buffer and its barriers
-        // rows whose segment has this thread's key as a live key in this tile
-        uint64_t live_rows = 0;
-#pragma unroll 1
-        for (int s = 0; s < nseg; ++s) {
-          const int* sw = w + 4 + s * kSegWords;
-          const int lo = sw[F_KT], keys = slot_keys(w, s, j);
-          if (kk >= lo && kk < lo + keys) live_rows |= row_mask(sw[F_ROW0], sw[F_ROWS]);
-        }
+        const uint64_t live_rows = single ? (kk < keys_total - j * kKeys ? single_mask : 0ull) : packed_rows;
         const bool ok = alive && warp_wait(&s_full[sb], (g / kLook) & 1, p.status);
         const uint32_t s_addr = lane_base + uint32_t(sb) * N;
         uint32_t keep[CW];          // scores of the first (for R <= 16: the only) column group

@@ -29,6 +29,7 @@ struct SegParams {
   int32_t num_q_heads, num_kv_heads, group;
   int32_t num_kn_tasks, num_kn_segs, kn_ctas;
   float scale_log2;          // log2(e) / sqrt(D)
+  uint32_t gmul;             // ceil(65536 / group): x / group == (x * gmul) >> 16 for x < 65536 / group
 };
 
 // One piece resolved against the (possibly updated) job lengths.

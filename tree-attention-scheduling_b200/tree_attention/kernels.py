@@ -164,7 +164,7 @@ KN_PACK_SEGS = 4     # segments of a packed tile
 def pack_segments(items):
     """Group keys-in-lanes segments into tasks.
 
-    ``items`` are ``(head, rows, slot, k0, keys, job_flags, first_request)``.  A segment of more
+    ``items`` are ``(head, rows, first_partial_row, k0, keys, job_flags, first_request)``.  A segment of more
     than one 128-key tile is a task of its own; shorter ones are packed, best
     fit by their 32-key-rounded span, into tiles of 128 keys, at most
     KN_PACK_SEGS segments and KN_PACK_ROWS query rows each (a segment of more
@@ -284,7 +284,7 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
             reqs = jobs[i].requests
             q0 = reqs[0] if reqs[-1] - reqs[0] + 1 == len(reqs) else -1
             for h in range(heads):
-                items.append((h, rows[i], int(pieces[p, 3]), jobs[i].tokens[0] + offset, take, i | (growing << 30),
+                items.append((h, rows[i], int(pieces[p, 3]) * groups, jobs[i].tokens[0] + offset, take, i | (growing << 30),
                               q0))
         elif route[i] == "tc":
             tc.extend((p, t) for t in range(ceil(rows[i] / TC_ROWS)))
@@ -303,8 +303,8 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
     for task in tasks:
         headers.append((len(segs), len(task), 0, 0))
         row0, kt = 0, 0
-        for h, r, first_slot, k0, keys, job, q0 in task:
-            segs.append((h, row0, r, first_slot, k0, kt if len(task) > 1 else 0, keys, job, q0, 0, 0, 0))
+        for h, r, first_row, k0, keys, job, q0 in task:
+            segs.append((h, row0, r, first_row, k0, kt if len(task) > 1 else 0, keys, job, q0, 0, 0, 0))
             row0 += r
             kt += -(-keys // KN_BOX) * KN_BOX
         costs.append(_tiles(max(s[4] for s in task)) + 1)
