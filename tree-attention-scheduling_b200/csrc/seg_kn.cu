@@ -114,18 +114,6 @@ __device__ __forceinline__ TaskR load_task(const int* w) {
   return t;
 }
 
-__device__ __forceinline__ void store_task(int* w, const TaskR& t) {
-  int4* v = reinterpret_cast<int4*>(w);
-  v[0] = make_int4(t.nseg, t.ntiles, t.rows, t.flags);
-#pragma unroll
-  for (int s = 0; s < kSegMax; ++s) {
-    const SegR& g = t.seg[s];
-    v[1 + 3 * s] = make_int4(g.head, g.row0, g.rows, g.nk);
-    v[2 + 3 * s] = make_int4(g.kt, g.span, g.job, g.k0);
-    v[3 + 3 * s] = make_int4(g.prow0, g.q0, 0, 0);
-  }
-}
-
 template <int R>
 struct KnCfg {
   static constexpr int N = R < 16 ? 16 : R;                 // MMA N

@@ -10,7 +10,7 @@
 //   warp 0      TMA producer of K tiles (token-major pool, 2 x 64-column boxes
 //               with 128-byte swizzle, no multicast), 2-stage ring (an optional
 //               L2 prefetch kPrefetch tiles ahead is off by default)
-//   warp 10     TMA producer of V tiles, likewise; it also zeroes the rows of
+//   warp 2      TMA producer of V tiles, likewise; it also zeroes the rows of
 //               the segment's last V tile that lie past the segment
 //   warp 1      one thread issues every tcgen05.mma: S_t = Q_t K^T (A = Q_t and
 //               B = K from shared memory) and O_t += P_t V (A = P_t from TMEM,
@@ -18,15 +18,17 @@
 //               in the order S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) ...
 //               so the tensor pipe works on one tile while softmax works on the
 //               other
-//   warps 2-9   softmax: two threads per query row (TMEM lane), each owning 64
-//               key columns, alternating between tiles A and B; row maxima are
-//               exchanged through shared memory with a named barrier per lane
-//               quadrant; exp2 on pre-scaled scores, a third of them by a
-//               polynomial on the FMA pipe; P packed to bf16/f16 pairs and
-//               stored to TMEM.  O_t is rescaled in TMEM only when a row's
-//               running max grows by more than 2^8 (otherwise the stale max is
-//               kept, which is exact after the final division).  Epilogue:
-//               O_t / z and the natural-log LSE per row.
+//   warps 3-6   softmax of tile A, warps 7-10 of tile B (a warp reaches the
+//               TMEM lane quadrant warp % 4): one thread per query
+//               row (TMEM lane) holding the row's 128 scores, so row maxima and
+//               sums stay in the thread; the two warpgroups run concurrently
+//               (one warp of each on every SM sub-partition).  exp2 on
+//               pre-scaled scores, a third of them by a polynomial on the FMA
+//               pipe; P packed to bf16/f16 pairs and stored to TMEM over S.
+//               O_t is rescaled in TMEM only when a row's running max grows by
+//               more than 2^8 (otherwise the stale max is kept, which is exact
+//               after the final division).  Epilogue: O_t / z and the
+//               natural-log LSE per row.
 //
 // Ordering facts the barrier scheme relies on: tcgen05.mma operations issued
 // by one thread execute in issue order, so S_t(j+1) cannot overwrite P_t(j)
@@ -53,10 +55,10 @@ constexpr int kDim = 128;       // head_dim (MMA K of S, N of P.V)
 constexpr int kKStages = 2;
 constexpr int kVStages = 2;
 constexpr int kPrefetch = 0;   // L2 prefetch distance in tiles (0: off; a 6-tile burst delayed the first loads)
+constexpr int kSoftmaxWarp0 = 3;          // warps 3-6: tile A, 7-10: tile B
 constexpr int kSoftmaxWarps = 8;
-constexpr int kVProducerWarp = 2 + kSoftmaxWarps;
-constexpr int kThreads = (3 + kSoftmaxWarps) * 32;
-constexpr int kHalfCols = kKeys / 2;                     // key columns per softmax thread
+constexpr int kVProducerWarp = 2;
+constexpr int kThreads = (kSoftmaxWarp0 + kSoftmaxWarps) * 32;
 constexpr uint32_t kTileBytes = kKeys * kDim * 2;       // 32 KB per K, V or Q tile
 constexpr uint32_t kHalfBytes = kTileBytes / 2;         // one 64-column swizzled block
 constexpr uint32_t kTmemCols = 512;
@@ -67,19 +69,16 @@ struct TcSmem {
   static constexpr uint32_t off_q = 0;                                 // Q_A, Q_B
   static constexpr uint32_t off_k = off_q + 2 * kTileBytes;
   static constexpr uint32_t off_v = off_k + kKStages * kTileBytes;
-  // [tile][3 slots][2 half][128 rows] f32: slots 0/1 row maxima by tile
-  // parity, slot 2 denominators
-  static constexpr uint32_t off_xchg = off_v + kVStages * kTileBytes;
-  static constexpr uint32_t off_bar = off_xchg + 2 * 3 * 2 * kRows * 4;
+  static constexpr uint32_t off_bar = off_v + kVStages * kTileBytes;
   static constexpr int kBars = 18;
   static constexpr uint32_t off_tmem = off_bar + kBars * 8;
   static constexpr uint32_t bytes = off_tmem + 16;
   static constexpr uint32_t alloc = bytes + 1024;         // slack to align the base to 1 KB
 };
 
-// k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[A,B], p_full[A,B], pv_done[A,B], q_full, v_tail
+// k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[A,B], p_full[A,B], pv_done[A,B], q_full[A,B], v_tail
 enum Bar {
-  K_FULL = 0, K_EMPTY = 2, V_FULL = 4, V_EMPTY = 6, S_FULL = 8, P_FULL = 10, PV_DONE = 12, Q_FULL = 14, V_TAIL = 15
+  K_FULL = 0, K_EMPTY = 2, V_FULL = 4, V_EMPTY = 6, S_FULL = 8, P_FULL = 10, PV_DONE = 12, Q_FULL = 14, V_TAIL = 16
 };
 
 // Instruction descriptor of this kernel's MMAs: M = 128 query rows, N = 128
@@ -89,13 +88,15 @@ __host__ __device__ constexpr uint32_t instr_desc(uint32_t ab_format, uint32_t b
   return umma_idesc(ab_format, 0, b_mn_major, kRows, kKeys);
 }
 
-// Maximum of 64 values as a balanced tree (short dependency chains).
-__device__ __forceinline__ float max64(const float (&s)[kHalfCols]) {
-  float m[8];
+// Maximum of 128 values as a balanced tree (short dependency chains).
+__device__ __forceinline__ float max128(const float (&s)[kKeys]) {
+  float m[16];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = fmaxf(fmaxf(s[i], s[i + 8]), fmaxf(s[i + 16], s[i + 24]));
+  for (int i = 0; i < 16; ++i) m[i] = fmaxf(fmaxf(s[i], s[i + 16]), fmaxf(s[i + 32], s[i + 48]));
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], fmaxf(fmaxf(s[i + 32], s[i + 40]), fmaxf(s[i + 48], s[i + 56])));
+  for (int i = 0; i < 16; ++i) m[i] = fmaxf(m[i], fmaxf(fmaxf(s[i + 64], s[i + 80]), fmaxf(s[i + 96], s[i + 112])));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], m[i + 8]);
   return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
 }
 
@@ -135,7 +136,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::off_bar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::off_tmem);
-  float* xchg = reinterpret_cast<float*>(smem + TcSmem::off_xchg);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int task = blockIdx.x, head = blockIdx.y;
@@ -173,10 +173,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars[V_FULL + s], 1);
       mbar_init(&bars[V_EMPTY + s], 1);
       mbar_init(&bars[S_FULL + s], 1);
-      mbar_init(&bars[P_FULL + s], kSoftmaxWarps);
+      mbar_init(&bars[P_FULL + s], kSoftmaxWarps / 2);
       mbar_init(&bars[PV_DONE + s], 1);
+      mbar_init(&bars[Q_FULL + s], kSoftmaxWarps / 2);
     }
-    mbar_init(&bars[Q_FULL], kSoftmaxWarps);
     mbar_init(&bars[V_TAIL], 1);
     fence_barrier_init();
   }
@@ -281,7 +281,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (alive) {
         tc_fence_after();
         issue_s(0, 0);
-        if (ntile == 2) issue_s(1, 0);
+        if (ntile == 2) {
+          if (mbar_wait(&bars[Q_FULL + 1], 0, p.status)) {
+            tc_fence_after();
+            issue_s(1, 0);
+          } else {
+            alive = false;
+          }
+        }
         umma_commit(&bars[K_EMPTY]);
       }
       for (int j = 0; j < ntiles && alive; ++j) {
@@ -316,139 +323,127 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&bars[V_EMPTY + j % kVStages], (j / kVStages) & 1, p.status)) break;
       }
     }
-  } else if (warp >= 2 && warp < 2 + kSoftmaxWarps) {
+  } else if (warp >= kSoftmaxWarp0) {
     // ---------------- softmax / correction / epilogue ----------------
+    // Warpgroup t (warps 3-6: tile A, 7-10: tile B); one thread per query row
+    // (TMEM lane), holding the row's 128 scores of a K tile in registers, so
+    // the row maximum and sum need no exchange between threads.
+    const int t = (warp - kSoftmaxWarp0) >> 2;
     const int quad = warp & 3;                       // TMEM lane quadrant of this warp
-    const int half = (warp - 2) >> 2;                // which 64 key columns of the row
-    const int row = quad * 32 + lane;                // query row of this thread within a tile
+    const int row = quad * 32 + lane;                // query row of this thread within its tile
+    const int trow = t * kRows + row;                // row within the pair
     const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);
-
-    // Q half-rows of both tiles -> shared memory (K-major, 128B swizzle),
-    // zero for padding rows.
-    for (int t = 0; t < 2; ++t) {
-      unsigned char* qs = smem + TcSmem::off_q + t * kTileBytes;
-      const int trow = t * kRows + row;              // row within the pair
-      const uint4* src = nullptr;
-      if (trow < rows) {
-        const int grow = r0 + trow;
-        const int rid = p.qids[int64_t(job) * p.max_requests + grow / G];
-        if (rid >= 0 && rid < p.num_requests)
-          src = reinterpret_cast<const uint4*>(p.q + (int64_t(rid) * p.num_q_heads + head * G + grow % G) * kDim);
-        else
-          set_status(p.status, TA_ERR_BOUNDS);
-      }
+    const uint32_t s_col = kColS + t * kKeys, o_col = kColO + t * kDim;
+    if (t < ntile) {
+      // this row of Q -> shared memory (K-major, 128B swizzle), zero for padding rows
+      {
+        unsigned char* qs = smem + TcSmem::off_q + t * kTileBytes;
+        const uint4* src = nullptr;
+        if (trow < rows) {
+          const int grow = r0 + trow;
+          const int rid = p.qids[int64_t(job) * p.max_requests + grow / G];
+          if (rid >= 0 && rid < p.num_requests)
+            src = reinterpret_cast<const uint4*>(p.q + (int64_t(rid) * p.num_q_heads + head * G + grow % G) * kDim);
+          else
+            set_status(p.status, TA_ERR_BOUNDS);
+        }
+        uint4 v[16];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const int chunk = half * 8 + c;
-        const uint4 v = src ? src[chunk] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(qs + swz_offset(row, chunk)) = v;
+        for (int c = 0; c < 16; ++c) v[c] = src ? src[c] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4*>(qs + swz_offset(row, c)) = v[c];
       }
-    }
-    fence_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&bars[Q_FULL]);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[Q_FULL + t]);
 
-    const float scale = p.scale_log2;
-    float m_run[2] = {-INFINITY, -INFINITY}, z[2] = {0.f, 0.f};
-    for (int j = 0; j < ntiles && alive; ++j) {
-      const int valid = min(kKeys, nk - j * kKeys) - half * kHalfCols;   // may be <= 0 for the upper half
-      for (int t = 0; t < ntile; ++t) {
-        const uint32_t s_col = kColS + t * kKeys;
-        float* my_x = xchg + t * (3 * 2 * kRows);    // [slot][half][row] of this tile
+      const float scale = p.scale_log2;
+      float m_run = -INFINITY, z = 0.f;
+      for (int j = 0; j < ntiles && alive; ++j) {
+        const int valid = min(kKeys, nk - j * kKeys);
         if (!warp_wait(&bars[S_FULL + t], j & 1, p.status)) { alive = false; break; }
         tc_fence_after();
-        float s[kHalfCols];
+        float s[kKeys];
         {
-          uint32_t a[32], b[32];
-          tmem_ld32(lane_addr + s_col + half * kHalfCols, a);
-          tmem_ld32(lane_addr + s_col + half * kHalfCols + 32, b);
-          tmem_wait_ld();
+          uint32_t a[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            s[i] = __uint_as_float(a[i]);
-            s[i + 32] = __uint_as_float(b[i]);
+          for (int c = 0; c < 4; ++c) {
+            tmem_ld32(lane_addr + s_col + c * 32, a);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(a[i]);
           }
         }
-        if (valid < kHalfCols) {
+        if (valid < kKeys) {
 #pragma unroll
-          for (int i = 0; i < kHalfCols; ++i)
+          for (int i = 0; i < kKeys; ++i)
             if (i >= valid) s[i] = -INFINITY;
         }
-        // row max across the two halves (both threads have finished reading S,
-        // so P may overwrite it after this barrier)
-        const int slot = j & 1;
-        my_x[(slot * 2 + half) * kRows + row] = max64(s);
-        named_sync(1 + quad, 64);
-        const float mx = fmaxf(my_x[(slot * 2 + 0) * kRows + row], my_x[(slot * 2 + 1) * kRows + row]);
-        const float m_tile = mx * scale;             // at least one key is valid: finite
-        float m_new = m_run[t];
+        const float m_tile = max128(s) * scale;      // at least one key is valid: finite
+        float m_new = m_run;
         bool rescale = false;
         if (j == 0) {
           m_new = m_tile;
-        } else if (m_tile > m_run[t] + kRescaleThreshold) {
+        } else if (m_tile > m_run + kRescaleThreshold) {
           m_new = m_tile;
           rescale = true;
         }
-        if (__any_sync(0xffffffffu, rescale)) {
-          // O_t holds P_t(j-1) V(j-1) already: S_t(j) was issued after it.
-          const float alpha = rescale ? fast_exp2(m_run[t] - m_new) : 1.f;
-          z[t] *= alpha;
+        const float alpha = rescale ? fast_exp2(m_run - m_new) : 1.f;
+        z *= alpha;
+        m_run = m_new;
+        F2 sum = splat(0.f);
+        const F2 sc = splat(scale), neg_m = splat(-m_new);
+        // P over the row: key columns [32h, 32h+32) -> packed columns [16h, 16h+16)
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
+        for (int h = 0; h < 4; ++h) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            F2 x;
+            x.f = make_float2(s[32 * h + 2 * i], s[32 * h + 2 * i + 1]);
+            x = ffma2(x, sc, neg_m);
+            F2 e;
+            if ((16 * h + i) % 3 == 2) {    // every third pair on the FMA pipe, the rest on the SFU
+              e = poly_exp2x2(x);
+            } else {
+              e.f = make_float2(fast_exp2(x.f.x), fast_exp2(x.f.y));
+            }
+            sum = fadd2(sum, e);
+            packed[i] = Elem<T>::pack2(e.f.x, e.f.y);
+          }
+          tmem_st16(lane_addr + s_col + h * 16, packed);
+        }
+        z += sum.f.x + sum.f.y;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O_t holds P_t(j-1) V(j-1) already (S_t(j) was issued after it);
+          // P_t(j) V(j) is not issued before this thread's P_FULL arrival.
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
-            tmem_ld32(lane_addr + kColO + t * kDim + half * kHalfCols + c * 32, o);
+            tmem_ld32(lane_addr + o_col + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(lane_addr + kColO + t * kDim + half * kHalfCols + c * 32, o);
+            tmem_st32(lane_addr + o_col + c * 32, o);
           }
         }
-        m_run[t] = m_new;
-        uint32_t packed[32];
-        F2 sum = splat(0.f);
-        const F2 sc = splat(scale), neg_m = splat(-m_new);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          F2 x;
-          x.f = make_float2(s[2 * i], s[2 * i + 1]);
-          x = ffma2(x, sc, neg_m);
-          F2 e;
-          if (i % 3 == 2) {               // every third pair on the FMA pipe, the rest on the SFU
-            e = poly_exp2x2(x);
-          } else {
-            e.f = make_float2(fast_exp2(x.f.x), fast_exp2(x.f.y));
-          }
-          sum = fadd2(sum, e);
-          packed[i] = Elem<T>::pack2(e.f.x, e.f.y);
-        }
-        z[t] += sum.f.x + sum.f.y;
-        // P over this thread's half of S_t: key columns [64h, 64h+64) ->
-        // packed columns [32h, 32h+32).
-        tmem_st32(lane_addr + s_col + half * 32, packed);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[P_FULL + t]);
       }
-    }
 
-    // epilogue per tile: wait for its last P.V, then O / z and the LSE.
-    // Observing S_t(ntiles-1) implied P_t(ntiles-2) V done, so PV_DONE_t is at
-    // most one phase behind this wait.
-    for (int t = 0; t < ntile; ++t) {
+      // epilogue: wait for the last P.V of this tile, then O / z and the LSE.
+      // Observing S_t(ntiles-1) implied P_t(ntiles-2) V done, so PV_DONE_t is
+      // at most one phase behind this wait.
       if (alive && !warp_wait(&bars[PV_DONE + t], (ntiles - 1) & 1, p.status)) alive = false;
       tc_fence_after();
-      float* my_x = xchg + t * (3 * 2 * kRows);
-      my_x[(4 + half) * kRows + row] = z[t];
-      named_sync(1 + quad, 64);
-      const float z_all = my_x[(4 + 0) * kRows + row] + my_x[(4 + 1) * kRows + row];
-      const float inv = (alive && z_all > 0.f) ? 1.f / z_all : 0.f;
-      const int trow = t * kRows + row;
-      float* dst = p.part + (head_rows + part_row0 + trow) * kDim + half * kHalfCols;
+      const float inv = (alive && z > 0.f) ? 1.f / z : 0.f;
+      float* dst = p.part + (head_rows + part_row0 + trow) * kDim;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
-        tmem_ld32(lane_addr + kColO + t * kDim + half * kHalfCols + c * 32, o);
+        tmem_ld32(lane_addr + o_col + c * 32, o);
         tmem_wait_ld();
         if (trow < rows) {
 #pragma unroll
@@ -458,9 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
         }
       }
-      if (trow < rows && half == 0)
-        p.lse[head_rows + part_row0 + trow] =
-            (alive && z_all > 0.f) ? (m_run[t] + fast_log2(z_all)) * kLn2 : -INFINITY;
+      if (trow < rows)
+        p.lse[head_rows + part_row0 + trow] = (alive && z > 0.f) ? (m_run + fast_log2(z)) * kLn2 : -INFINITY;
     }
   }
 
