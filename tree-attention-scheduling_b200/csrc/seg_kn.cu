@@ -341,6 +341,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     // task k-1) and the header of task k+2 are in flight.
     int4* stage = reinterpret_cast<int4*>(smem + C::off_stage);     // [2][3 * kSegMax]
     int64_t* rowsrc = reinterpret_cast<int64_t*>(smem + C::off_rowsrc);
+    int pending_qb = -1;           // Q^T buffer whose copies are issued but not yet published
+    auto flush = [&]() {
+      if (pending_qb >= 0) {
+        cp_async_wait_group<0>();
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full[pending_qb]);
+        pending_qb = -1;
+      }
+    };
+    // Bounded wait that first publishes the pending Q^T if the phase is not complete yet.
+    auto wait_or_flush = [&](uint64_t* bar, uint32_t parity) -> bool {
+      int ok = 1;
+      if (lane == 0) ok = mbar_test_wait(bar, parity);
+      if (__shfl_sync(0xffffffffu, ok, 0)) return true;
+      flush();
+      if (lane == 0) ok = mbar_wait(bar, parity, p.status);
+      return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    };
     auto header_ok = [&](int4 h) { return h.y >= 1 && h.y <= kSegMax && h.x >= 0 && int64_t(h.x) + h.y <= p.num_kn_segs; };
     int4 hdr = count > 0 ? load_header(p, begin) : make_int4(0, 0, 0, 0);
     if (count > 0 && header_ok(hdr) && lane < 3 * hdr.y)
@@ -354,11 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool pre_ok = k + 1 < count && header_ok(hdr_next) && lane < 3 * hdr_next.y;
       if (pre_ok) pre = reinterpret_cast<const int4*>(p.kn_segs)[3 * int64_t(hdr_next.x) + lane];
       const int4 hdr_after = k + 2 < count ? load_header(p, begin + k + 2) : make_int4(0, 0, 0, 0);
-      if (k >= kTQ) {
-        int ok = 1;
-        if (lane == 0) ok = mbar_wait(&task_empty[k % kTQ], ((k / kTQ) - 1) & 1, p.status);
-        if (!__shfl_sync(0xffffffffu, ok, 0)) { alive = false; break; }
-      }
+      if (k >= kTQ && !wait_or_flush(&task_empty[k % kTQ], ((k / kTQ) - 1) & 1)) { alive = false; break; }
       decode_task<R>(p, header_ok(hdr) ? hdr.y : 0, stage + (k & 1) * 3 * kSegMax, w, lane);
       __syncwarp();
       if (lane == 0) mbar_arrive(&task_full[k % kTQ]);
@@ -369,14 +384,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TaskR t = load_task(w);
       if (t.nseg == 0 || t.ntiles == 0) continue;    // no tiles: no Q^T
       const int qb = qi % QB;
-      if (qi >= QB) {
-        int ok = 1;
-        if (lane == 0) ok = mbar_wait(&q_empty[qb], ((qi / QB) - 1) & 1, p.status);
-        if (!__shfl_sync(0xffffffffu, ok, 0)) { alive = false; break; }
-      }
+      if (qi >= QB && !wait_or_flush(&q_empty[qb], ((qi / QB) - 1) & 1)) { alive = false; break; }
       // Each lane finds the Q row behind tile rows lane and lane + 32, then the
-      // warp copies rows x 16 chunks of 16 bytes, swizzled K-major: loads
-      // first, stores after.
+      // warp copies rows x 16 chunks of 16 bytes, swizzled K-major, with
+      // asynchronous copies (zero-filled where a row is out of range).  This
+      // task's Q^T is published once the next task's copies are issued (or
+      // before the warp blocks), so the copy latency of consecutive tasks
+      // overlaps.
       const int rows = t.rows;
       for (int r = lane; r < rows; r += 32) {
         SegR sg = t.seg[0];
@@ -395,31 +409,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       unsigned char* dst = qbuf + qb * C::kQBytes;
-      for (int e0 = 0; e0 < rows * 16; e0 += 4 * 32) {
-        uint4 v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = e0 + u * 32 + lane;
-          v[u] = make_uint4(0, 0, 0, 0);
-          if (e < rows * 16) {
-            const int64_t s = rowsrc[e >> 4];
-            if (s >= 0) v[u] = *reinterpret_cast<const uint4*>(p.q + s + (e & 15) * 8);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = e0 + u * 32 + lane;
-          if (e < rows * 16) {
-            const int r = e >> 4, c = e & 15;
-            *reinterpret_cast<uint4*>(dst + (c >> 3) * C::kQHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v[u];
-          }
-        }
+      for (int e = lane; e < rows * 16; e += 32) {
+        const int r = e >> 4, c = e & 15;
+        const int64_t s = rowsrc[r];
+        cp_async16_zfill(dst + (c >> 3) * C::kQHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4),
+                         s >= 0 ? p.q + s + c * 8 : p.q, s >= 0 ? 16u : 0u);
       }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&q_full[qb]);
+      cp_async_commit();
+      if (pending_qb >= 0) {             // the previous task's copies: the older group
+        cp_async_wait_group<1>();
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full[pending_qb]);
+      }
+      pending_qb = qb;
       ++qi;
     }
+    flush();
   } else if (warp == kKWarp || warp == kVWarp) {
     // ---------------- TMA producers ----------------
     if (lane == 0) {
@@ -477,43 +483,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pdesc0 = smem_desc(smem_u32(smem + C::off_p), 16, 1024);
       bool alive = true;
 
-      // Two cursors over the CTA's tiles: `sc` issues S kLook tiles ahead of `pc`.
-      // Tasks without tiles are skipped; `qi` counts the tasks with tiles,
-      // which alone use the Q^T and O^T buffers.  The S cursor waits for each
-      // task slot; the P.V cursor, which trails it, releases every slot.
+      // Two cursors over the CTA's tiles: `sc` issues S up to kLook tiles ahead
+      // of `pc`, which issues P.V.  The loop polls: whichever of the two has
+      // its inputs in goes first, so a P.V never waits behind the inputs of a
+      // later S (a later task's Q^T or K tile) and vice versa.  Tasks without
+      // tiles are skipped; `qi` counts the tasks with tiles, which alone use
+      // the Q^T and O^T buffers.  The S cursor waits for each task slot; the
+      // P.V cursor, which trails it, copies each slot and releases it.
       struct Cursor {
         int k, j, g, qi;      // index within the list, tile in task, global tile, index among tasks with tiles
         TaskR t;
       };
-      // The lead (S) cursor waits for each task slot; the trailing (P.V)
-      // cursor copies it to registers and releases it for the MMA warp.
-      auto settle = [&](Cursor& c, bool lead) {   // move to the next task with tiles
-        while (c.k < count) {
-          if (lead && !mbar_wait(&task_full[c.k % kTQ], (c.k / kTQ) & 1, p.status)) {
-            alive = false;
-            c.k = count;
-            return;
-          }
-          c.t = load_task(slot_of(c.k));
-          if (!lead) mbar_arrive(&task_empty[c.k % kTQ]);
-          if (c.t.nseg > 0 && c.t.ntiles > 0) return;
-          ++c.k;
-        }
-      };
-      auto advance = [&](Cursor& c, bool lead) {
-        ++c.g;
-        if (++c.j >= c.t.ntiles) {
-          c.j = 0;
-          ++c.k;
-          ++c.qi;
-          settle(c, lead);
-        }
-      };
-      auto issue_s = [&](const Cursor& c) -> bool {
+      auto issue_s = [&](const Cursor& c) {
         const int st = c.g % S;
-        if (c.j == 0 && !mbar_wait(&q_full[c.qi % QB], (c.qi / QB) & 1, p.status)) return false;
-        if (!mbar_wait(&k_full[st], (c.g / S) & 1, p.status)) return false;
-        tc_fence_after();
         const uint64_t kd = kdesc0 + ((uint64_t(st) * kTileBytes) >> 4);
         const uint64_t qd = qdesc0 + ((uint64_t(c.qi % QB) * C::kQBytes) >> 4);
         const uint32_t d = tmem + uint32_t(c.g % kLook) * N;
@@ -526,14 +508,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&s_full[c.g % kLook]);
         umma_commit(&k_empty[st]);
         if (c.j == c.t.ntiles - 1) umma_commit(&q_empty[c.qi % QB]);   // the task's last S: its Q^T buffer is free
-        return true;
       };
       // P.V reads key rows [0, 16 * steps); every such row that is not a live
       // key of its slot is zeroed first.
-      auto issue_pv = [&](const Cursor& c) -> bool {
+      auto issue_pv = [&](const Cursor& c) {
         const int st = c.g % S;
-        if (!mbar_wait(&p_full[c.g % kLook], (c.g / kLook) & 1, p.status)) return false;
-        if (!mbar_wait(&v_full[st], (c.g / S) & 1, p.status)) return false;
         const TaskR& t = c.t;
         int steps = 8;
         if (t.nseg > 1 || seg_keys(t, 0, c.j) < kKeys) {
@@ -572,29 +551,95 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&v_empty[st]);
         umma_commit(&pv_done[c.g % kLook]);
-        return true;
       };
 
       Cursor sc, pc;
       sc.k = sc.j = sc.g = sc.qi = 0;
       pc.k = pc.j = pc.g = pc.qi = 0;
-      settle(sc, true);
-      for (int k = 0; k < kLook && sc.k < count && alive; ++k) {
-        alive = issue_s(sc);
-        advance(sc, true);
-      }
-      if (alive) settle(pc, false);
-      // P.V(g) as soon as its inputs are in, then S(g+3).  P.V(g) must not wait
-      // for S(g+3)'s inputs: those depend on softmax progress that waits for P.V(g).
-      while (pc.k < count && alive) {
-        alive = issue_pv(pc);
-        if (!alive) break;
-        advance(pc, false);
-        if (sc.k < count) {
-          alive = issue_s(sc);
-          advance(sc, true);
+      bool s_loaded = false, p_loaded = false;
+      // Lead: point sc at a waited-for task with tiles, without blocking.
+      // False while its slot is not published or when no task is left.
+      auto lead_ready = [&]() -> bool {
+        while (sc.k < count) {
+          if (!s_loaded) {
+            if (!mbar_test_wait(&task_full[sc.k % kTQ], (sc.k / kTQ) & 1)) return false;
+            sc.t = load_task(slot_of(sc.k));
+            s_loaded = true;
+          }
+          if (sc.t.nseg > 0 && sc.t.ntiles > 0) return true;
+          ++sc.k;
+          s_loaded = false;
+        }
+        return false;
+      };
+      // Trail: copy and release every slot up to the next task with tiles.
+      // Only called for slots the lead has already waited for.
+      auto trail_settle = [&]() {
+        while (pc.k < count && !p_loaded) {
+          pc.t = load_task(slot_of(pc.k));
+          mbar_arrive(&task_empty[pc.k % kTQ]);
+          if (pc.t.nseg > 0 && pc.t.ntiles > 0) {
+            p_loaded = true;
+            break;
+          }
+          ++pc.k;
+        }
+      };
+      uint64_t idle_since = 0;
+      while (alive) {
+        bool did = false;
+        if (pc.g < sc.g) {                              // P.V of the oldest tile whose S is issued
+          if (!p_loaded) trail_settle();
+          const int st = pc.g % S;
+          if (mbar_test_wait(&p_full[pc.g % kLook], (pc.g / kLook) & 1) &&
+              mbar_test_wait(&v_full[st], (pc.g / S) & 1)) {
+            issue_pv(pc);
+            ++pc.g;
+            if (++pc.j >= pc.t.ntiles) {
+              pc.j = 0;
+              ++pc.k;
+              ++pc.qi;
+              p_loaded = false;
+            }
+            did = true;
+          }
+        }
+        if (sc.g - pc.g < kLook && lead_ready()) {       // S of the next tile, up to kLook ahead
+          const int st = sc.g % S;
+          if ((sc.j != 0 || mbar_test_wait(&q_full[sc.qi % QB], (sc.qi / QB) & 1)) &&
+              mbar_test_wait(&k_full[st], (sc.g / S) & 1)) {
+            tc_fence_after();
+            issue_s(sc);
+            ++sc.g;
+            if (++sc.j >= sc.t.ntiles) {
+              sc.j = 0;
+              ++sc.k;
+              ++sc.qi;
+              s_loaded = false;
+            }
+            did = true;
+          }
+        }
+        if (sc.k >= count && pc.g == sc.g) break;        // every tile issued and its P.V too
+        if (did) {
+          idle_since = 0;
+        } else {
+          // nothing ready: rest on the oldest pending P.V (or briefly) rather
+          // than taking issue slots from the softmax warp on this sub-partition
+          if (pc.g < sc.g)
+            mbar_try_wait_for(&p_full[pc.g % kLook], (pc.g / kLook) & 1, 200);
+          else
+            __nanosleep(64);
+          const uint64_t now = global_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > TA_WAIT_NS) {
+            set_status(p.status, TA_ERR_TIMEOUT);
+            alive = false;
+          }
         }
       }
+      if (alive) trail_settle();                          // release the trailing slots without tiles
       // The last commits must land before the CTA's shared memory is released.
       const int total = pc.g;
       if (alive) {
@@ -654,15 +699,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (o_ok) {
             tmem_ldw<CW>(lane_base + kLook * N + uint32_t(b) * N + c * CW, o);
             tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int q = 0; q < CW; ++q) o[q] = 0u;
           }
+          float inv[CW];
+#pragma unroll
+          for (int q = 0; q < CW; ++q) inv[q] = (o_ok && z[q] > 0.f) ? __fdividef(1.f, z[q]) : 0.f;
 #pragma unroll
           for (int q = 0; q < CW; ++q) {
             const int r = c * CW + q;
             if (r < rows) {
               const int64_t row = out_row(t, r);
-              const bool live = o_ok && z[q] > 0.f;
-              p.part[row * kDim + kk] = live ? __uint_as_float(o[q]) * (1.f / z[q]) : 0.f;
-              if (kk == r) p.lse[row] = live ? (mr[q] + fast_log2(z[q])) * kLn2 : -INFINITY;
+              p.part[row * kDim + kk] = __uint_as_float(o[q]) * inv[q];
+              if (kk == r) p.lse[row] = inv[q] > 0.f ? (mr[q] + fast_log2(z[q])) * kLn2 : -INFINITY;
             }
           }
         }
@@ -764,9 +814,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int q = 0; q < CW; ++q) {
                 const int r = c * CW + q;
-                wm[q] = (r < rows) ? warp_max_redux(((live_rows >> r) & 1ull) ? __uint_as_float(raw[q]) * scale
-                                                                                : -INFINITY)
-                                   : -INFINITY;
+                wm[q] = warp_max_redux(((live_rows >> r) & 1ull) ? __uint_as_float(raw[q]) * scale : -INFINITY);
               }
               if (lane == 0) {
 #pragma unroll
@@ -793,9 +841,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int r = c * CW + q;
                 const float mt = fmaxf(fmaxf(rt[r], rt[R + r]), fmaxf(rt[2 * R + r], rt[3 * R + r]));
                 const float mn = fmaxf(m[r], mt);
-                alpha[q] = (r < rows && mn != -INFINITY) ? fast_exp2(m[r] - mn) : 1.f;   // m = -inf gives 0
+                alpha[q] = mn != -INFINITY ? fast_exp2(m[r] - mn) : 1.f;   // m = -inf gives 0
                 l[r] *= alpha[q];
-                m[r] = r < rows ? mn : m[r];
+                m[r] = mn;                  // rows past `rows` have no live key and stay at -inf
               }
               if (o_ok) {
                 uint32_t o[CW];
@@ -832,8 +880,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 e16[q] = Elem<T>::from_float(e);
               }
 #pragma unroll
-              for (int q = 0; q < CW; ++q)
-                if (c * CW + q < rows) *reinterpret_cast<uint16_t*>(pt + swz(C::kQHalf, c * CW + q, kk)) = e16[q];
+              for (int q = 0; q < CW; ++q)            // rows past `rows` get P = 0
+                *reinterpret_cast<uint16_t*>(pt + swz(C::kQHalf, c * CW + q, kk)) = e16[q];
             }
           }
         }
@@ -852,13 +900,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = qi & 1;
         float* sl = suml + b * 4 * R;
         if constexpr (R <= 16) {
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            if (r < rows) {
-              const float s = warp_sum(l[r]);
-              if (lane == 0) sl[warp * R + r] = s;
-            }
-          }
+          // lane l ends with the warp's sum of row l >> (5 - log2 R)
+          constexpr int kShift = R == 4 ? 3 : (R == 8 ? 2 : 1);
+          const float s = warp_transpose_sum<R>(l, lane);
+          if ((lane & ((1 << kShift) - 1)) == 0) sl[warp * R + (lane >> kShift)] = s;
         } else {
 #pragma unroll
           for (int c = 0; c < R / 32; ++c) {

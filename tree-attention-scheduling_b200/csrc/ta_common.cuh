@@ -121,6 +121,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of phase `parity` of `bar` (for loops that poll several barriers).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// try_wait that suspends the thread for at most about `ns` nanoseconds.
+__device__ __forceinline__ bool mbar_try_wait_for(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -165,6 +191,29 @@ __device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) 
       v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
     }
   }
+  return v[0];
+}
+
+// Sums of W values (W = 4, 8 or 16) over the 32 lanes by recursive halving:
+// W - 1 + 5 - log2(W) shuffles.  Lane l returns the sum of v[l >> (5 - log2 W)].
+template <int W>
+__device__ __forceinline__ float warp_transpose_sum(const float (&in)[W], int lane) {
+  float v[W];
+#pragma unroll
+  for (int i = 0; i < W; ++i) v[i] = in[i];
+  int off = 16;
+#pragma unroll
+  for (int n = W; n > 1; n >>= 1, off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = upper ? v[i] : v[i + n / 2];
+      const float keep = upper ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+#pragma unroll
+  for (; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
   return v[0];
 }
 
