@@ -119,7 +119,10 @@ struct KnCfg {
   static constexpr int N = R < 16 ? 16 : R;                 // MMA N
   static constexpr int CW = R < 16 ? R : 16;                // TMEM columns per load
   static constexpr int NC = R / CW;                          // loads per row set
-  static constexpr int kStages = N <= 16 ? 3 : 2;
+  // Up to 8 rows: two CTAs per SM (one K and one V stage each, at most 128
+  // registers per thread) so two softmax chains interleave on every SM.
+  static constexpr int kCtasPerSm = R <= 8 ? 2 : 1;
+  static constexpr int kStages = kCtasPerSm == 2 ? 1 : (N <= 16 ? 3 : 2);
   static constexpr uint32_t kQHalf = N * 128;               // 64-column block of N rows
   static constexpr uint32_t kQBytes = 2 * kQHalf;           // Q^T or P^T buffer
   static constexpr uint32_t off_k = 0;
@@ -142,6 +145,7 @@ struct KnCfg {
   static constexpr uint32_t alloc = bytes + 1024;             // slack to align the base to 1 KB
   static constexpr uint32_t kTmemCols = N == 16 ? 128 : (N == 32 ? 256 : 512);   // S^T[kLook] + O^T[2]
   static_assert(alloc <= 227 * 1024, "shared memory budget");
+  static_assert(kCtasPerSm == 1 || alloc <= 113 * 1024, "two CTAs per SM");
   static_assert((kLook + 2) * N <= kTmemCols, "TMEM budget");
 };
 
@@ -266,7 +270,7 @@ __device__ __forceinline__ void tmem_stw(uint32_t taddr, const uint32_t (&r)[W])
 }
 
 template <typename T, int R>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
     seg_kn_kernel(SegParams p, const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v) {
   using C = KnCfg<R>;
   constexpr int N = C::N, CW = C::CW, NC = C::NC;

@@ -156,6 +156,11 @@ def split_pieces(jobs, groups, heads, use_tc, sms, no_split_from=None):
     return pieces, route, rows
 
 
+# Keys-in-lanes tasks of at most KN_DUAL_ROWS query rows run KN_DUAL_CTAS
+# persistent CTAs per SM (each with a single K and V stage), so two CTAs'
+# softmax chains interleave on every SM.
+KN_DUAL_ROWS = 8
+KN_DUAL_CTAS = 2
 KN_BOX = 32          # keys-in-lanes TMA box height: packed segments start on 32-key boundaries
 KN_PACK_ROWS = 16    # query rows of a packed tile
 KN_PACK_SEGS = 4     # segments of a packed tile
@@ -296,7 +301,6 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
     small_tasks = np.array([t for c in small for t in c], dtype=np.int32).reshape(-1, 2)
     tc_tasks = np.array(tc, dtype=np.int32).reshape(-1, 2)
     tasks = pack_segments(items)
-    kn_ctas = min(sms, len(tasks))
     segs = []
     headers = []
     costs = []
@@ -309,6 +313,7 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
             kt += -(-keys // KN_BOX) * KN_BOX
         costs.append(_tiles(max(s[4] for s in task)) + 1)
     kn_rows = max((sum(s[1] for s in task) for task in tasks), default=0)
+    kn_ctas = min(sms * (KN_DUAL_CTAS if kn_rows <= KN_DUAL_ROWS else 1), len(tasks))
     if tasks:
         kn_offsets, order = assign_lpt(costs, kn_ctas)
         kn_tasks = np.array(headers, dtype=np.int32)[order]
