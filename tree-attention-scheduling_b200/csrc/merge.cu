@@ -17,6 +17,7 @@ constexpr int kMergeWarps = 4;
 template <typename T, int D>
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) {
   constexpr int DL = D / 32;
+  pdl_wait();                // the segment kernels before this one have completed
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
   if (item >= p.num_requests * p.num_q_heads) return;
@@ -134,7 +135,8 @@ cudaError_t launch_merge_typed(const MergeParams& p, cudaStream_t stream) {
   const int items = p.num_requests * p.num_q_heads;
   if (items == 0) return cudaSuccess;
   const int blocks = (items + kMergeWarps - 1) / kMergeWarps;
-  merge_kernel<T, D><<<blocks, kMergeWarps * 32, 0, stream>>>(p);
+  cudaError_t err = launch_dependent(merge_kernel<T, D>, dim3(blocks), dim3(kMergeWarps * 32), 0, stream, p);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

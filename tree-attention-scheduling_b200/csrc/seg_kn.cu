@@ -294,6 +294,7 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::off_tmem);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_trigger();             // the merge may be placed early; it waits for this kernel's completion
   const int G = p.group;
   int begin = p.kn_offsets[blockIdx.x], end = p.kn_offsets[blockIdx.x + 1];
   if (begin < 0 || end < begin || end > p.num_kn_tasks) {
@@ -934,6 +935,10 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
   }
+  // This kernel may have started while the query-tile kernel before it was
+  // still running (it reads nothing that kernel writes); it completes only
+  // after that kernel, so whatever waits for this one also waits for both.
+  pdl_wait();
 }
 
 template <typename T, int R>
@@ -949,7 +954,8 @@ cudaError_t launch_r(const SegParams& p, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     configured = true;
   }
-  kernel<<<p.kn_ctas, kThreads, KnCfg<R>::alloc, stream>>>(p, tk, tv);
+  cudaError_t err = launch_dependent(kernel, dim3(p.kn_ctas), dim3(kThreads), KnCfg<R>::alloc, stream, p, tk, tv);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

@@ -138,6 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::off_tmem);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_trigger();             // the keys-in-lanes kernel may start on SMs this grid leaves free
   const int task = blockIdx.x, head = blockIdx.y;
   const int G = p.group;
 
@@ -440,17 +441,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv = (alive && z > 0.f) ? 1.f / z : 0.f;
       float* dst = p.part + (head_rows + part_row0 + trow) * kDim;
+      const bool part32 = (reinterpret_cast<uintptr_t>(p.part) & 31u) == 0;   // rows are 512 bytes
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
         tmem_ld32(lane_addr + o_col + c * 32, o);
         tmem_wait_ld();
         if (trow < rows) {
+          if (part32) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(dst + c * 32 + i) =
-                make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
-                            __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+            for (int i = 0; i < 32; i += 8) {     // full 32-byte sectors
+              float v[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) v[u] = __uint_as_float(o[i + u]) * inv;
+              st_global_v8(dst + c * 32 + i, v);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(dst + c * 32 + i) =
+                  make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                              __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+          }
         }
       }
       if (trow < rows)

@@ -155,6 +155,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+// 32-byte global store (sm_100 256-bit vector store): one full sector per thread.
+__device__ __forceinline__ void st_global_v8(float* dst, const float (&v)[8]) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "f"(v[0]), "f"(v[1]),
+               "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 // 16-byte copy that reads `src_bytes` (0 or 16) bytes and zero-fills the rest.
 __device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, uint32_t src_bytes) {
