@@ -37,17 +37,20 @@
  *   pcounts     [num_requests]              partials per request (over pieces)
  *   cslots      [num_requests, max_pslots]  partial slots of each request
  *   small_tasks [num_small_tasks, 2]        (piece, 16-row tile), SIMT kernel
- *   tc_tasks    [num_tc_tasks, 2]           (piece, 256-row pair), query-tile tcgen05 kernel
+ *   tc_tasks    [num_tc_tasks, 4]           (piece, 256-row pair, first request of the job if its
+ *                                           requests are contiguous else -1, 0), query-tile kernel
  *   kn_offsets  [kn_ctas + 1]               task range of each persistent CTA of the
  *                                           keys-in-lanes tcgen05 kernel
  *   kn_tasks    [num_kn_tasks, 4]           its task headers: first segment, segments, 0, 0
  *   kn_segs     [num_kn_segs, 12]           segments: KV head, first query row in the
- *                                           task, query rows, first partial row (slot * G), first
+ *                                           task, query rows, first partial row, first
  *                                           pool position, first key of its slot in the
  *                                           tile, keys, job | growing << 30 (growing: keys
  *                                           = min(keys, klen[job]), a decode tail), first
- *                                           request if the job's requests are contiguous
- *                                           (else -1), 0, 0, 0; a task of several
+ *                                           request if the segment's requests are contiguous
+ *                                           (else -1), index of the segment's first request
+ *                                           within its job (a job's rows may be cut into
+ *                                           several segments), 0, 0; a task of several
  *                                           segments is one 128-key tile
  * Every array starts at a multiple of 4 int32 (16 bytes).  Partial slot s of a
  * piece holds query rows s*G .. s*G+G-1 (one request).
@@ -66,7 +69,7 @@
 extern "C" {
 #endif
 
-#define TA_ABI_VERSION 3
+#define TA_ABI_VERSION 4
 
 #define TA_DTYPE_BF16 1
 #define TA_DTYPE_F16 2
@@ -94,8 +97,12 @@ typedef struct ta_plan_layout {
   int32_t num_tc_tasks;
   int32_t num_kn_tasks;
   int32_t num_kn_segs;
-  int32_t kn_ctas;       /* persistent CTAs of the keys-in-lanes kernel (<= SM count) */
-  int32_t kn_rows;       /* most query rows of any keys-in-lanes task (<= 64) */
+  int32_t kn_ctas;       /* persistent CTAs of the keys-in-lanes launches, all classes */
+  /* keys-in-lanes tasks are grouped by query rows into classes of at most 4,
+     8, 16, 32 and 64 rows, one launch per non-empty class; class c has
+     kn_class_ctas[c] persistent CTAs, whose kn_offsets entries follow those
+     of the classes before it (the sum is kn_ctas) */
+  int32_t kn_class_ctas[5];
   /* small tasks are sorted by padded row count: [0, e0) need 4 rows,
      [e0, e1) 8 rows, [e1, e2) 16 rows; e2 == num_small_tasks */
   int32_t small_class_end[3];

@@ -67,39 +67,44 @@ def check_b200_arrays(p, groups, heads=None):
     for piece, tile in meta["small_tasks"]:
         key = (int(piece), "s", int(tile))
         covered[key] = covered.get(key, 0) + 1
-    for piece, pair in meta["tc_tasks"]:
+    for piece, pair, q0, _ in meta["tc_tasks"]:
         key = (int(piece), "t", int(pair))
         covered[key] = covered.get(key, 0) + 1
+        job = int(pieces[piece][0])
+        reqs = qids[job, :qlen[job]].tolist()
+        assert q0 == (reqs[0] if reqs == list(range(reqs[0], reqs[0] + len(reqs))) else -1)
     slot_piece = {int(first): pc for pc, (_, _, _, first) in enumerate(pieces)}
     segs = meta["kn_segs"]
     for first, nseg, _, _ in meta["kn_tasks"]:
         assert 1 <= nseg <= kernels.KN_PACK_SEGS
         row0 = kt = 0
-        for head, r0, rows, prow, k0, seg_kt, keys, jobf, q0, _, _, _ in segs[first:first + nseg]:
+        for head, r0, rows, prow, k0, seg_kt, keys, jobf, q0, qofs, _, _ in segs[first:first + nseg]:
             job, growing = int(jobf) & 0x3FFFFFFF, int(jobf) >> 30
-            assert prow % groups == 0
-            pc = slot_piece[int(prow) // groups]
-            assert pieces[pc, 0] == job and keys == pieces[pc, 2] and rows == qlen[job] * groups
+            assert prow % groups == 0 and rows % groups == 0 and qofs * groups + rows <= qlen[job] * groups
+            pc = slot_piece[int(prow) // groups - int(qofs)]
+            assert pieces[pc, 0] == job and keys == pieces[pc, 2]
+            assert rows == min(max(groups, kernels.KN_TASK_ROWS // groups * groups), qlen[job] * groups - qofs * groups)
             assert k0 == p.jobs[job].tokens[0] + pieces[pc, 1] and growing in (0, 1)
             reqs = p.jobs[job].requests
-            assert q0 == (reqs[0] if reqs[-1] - reqs[0] + 1 == len(reqs) else -1)
+            assert q0 == (reqs[0] + qofs if reqs[-1] - reqs[0] + 1 == len(reqs) else -1)
             assert r0 == row0 and (nseg == 1 and seg_kt == 0 or seg_kt == kt)
             if nseg > 1:
                 assert keys <= kernels.KEY_TILE
             row0 += rows
             kt += -(-int(keys) // kernels.KN_BOX) * kernels.KN_BOX
-            key = (pc, "k", int(head))
+            key = (pc, "k", int(head), int(qofs))
             covered[key] = covered.get(key, 0) + 1
         if nseg > 1:
             assert kt <= kernels.KEY_TILE and row0 <= kernels.KN_PACK_ROWS
     assert all(v == 1 for v in covered.values())
     rows_covered = np.zeros(len(pieces), dtype=np.int64)
-    for (piece, kind, idx) in covered:
+    for (piece, kind, idx, *sub) in covered:
         rows = int(qlen[pieces[piece, 0]]) * groups
         if kind == "k":
-            assert rows <= kernels.KN_ROWS and all((piece, "k", h) in covered for h in range(heads))
+            chunk = max(groups, kernels.KN_TASK_ROWS // groups * groups)
+            assert rows <= kernels.KN_ROWS and all((piece, "k", h, sub[0]) in covered for h in range(heads))
             if idx == 0:
-                rows_covered[piece] += rows
+                rows_covered[piece] += min(chunk, rows - sub[0] * groups)
         else:
             size = kernels.SMALL_ROWS if kind == "s" else kernels.TC_ROWS
             if kind == "t":
@@ -118,8 +123,17 @@ def check_b200_arrays(p, groups, heads=None):
     offs = meta["kn_offsets"]
     assert offs[0] == 0 and offs[-1] == len(meta["kn_tasks"]) and np.all(np.diff(offs) >= 0)
     assert len(offs) == meta["kn_ctas"] + 1
-    if len(meta["kn_tasks"]):
-        assert meta["kn_rows"] == max(int(segs[f:f + n, 2].sum()) for f, n, _, _ in meta["kn_tasks"])
+    # CTAs of each row class hold only tasks of that class, classes in order
+    cc = meta["kn_class_ctas"]
+    assert int(cc.sum()) == meta["kn_ctas"]
+    assert [L.kn_class_ctas[c] for c in range(5)] == cc.tolist()
+    cta = 0
+    for c, n in enumerate(cc.tolist()):
+        for b in range(cta, cta + n):
+            assert offs[b + 1] > offs[b]                  # no idle CTA
+            for f, nseg, _, _ in meta["kn_tasks"][offs[b]:offs[b + 1]]:
+                assert kernels.kn_class(int(segs[f:f + nseg, 2].sum())) == c
+        cta += n
     assert all(getattr(L, "off_" + name) % 4 == 0 for name in ("pieces", "cslots", "kn_tasks", "kn_segs", "kn_offsets"))
     # layout offsets address the same arrays as the views
     flat = p.metadata.numpy()
@@ -144,7 +158,7 @@ def test_task_lists_cover_rows(use_tc, monkeypatch):
             meta = p.host_arrays
             if use_tc:
                 assert len(meta["small_tasks"]) == 0
-                assert all(meta["qlen"][meta["pieces"][pc, 0]] * 4 > kernels.KN_ROWS for pc, _ in meta["tc_tasks"])
+                assert all(meta["qlen"][meta["pieces"][pc, 0]] * 4 > kernels.KN_ROWS for pc, _, _, _ in meta["tc_tasks"])
             else:
                 assert len(meta["tc_tasks"]) == 0 and len(meta["kn_tasks"]) == 0
 
@@ -180,7 +194,8 @@ def test_pieces_split_long_jobs_and_keep_tails_whole():
     root = [pc for pc in meta["pieces"] if meta["qlen"][pc[0]] == 16]
     assert len(root) > 1 and sum(int(pc[2]) for pc in root) == 8192
     assert all(pc[2] % kernels.KEY_TILE == 0 for pc in root[:-1])
-    assert len(meta["kn_segs"]) == len(meta["pieces"]) * 8
+    chunk = kernels.KN_TASK_ROWS
+    assert len(meta["kn_segs"]) == sum(8 * -(-int(meta["qlen"][pc[0]]) * 4 // chunk) for pc in meta["pieces"])
     check_b200_arrays(p, 4)
     # decode tails (positions past the prompt) are never split and follow klen
     tails = [kernels.Job((r,), tuple(range(tree.storage_tokens + r * 4096, tree.storage_tokens + (r + 1) * 4096)))
@@ -211,10 +226,10 @@ def test_packing_shares_tiles_between_short_segments():
     meta = p.host_arrays
     counts = [int(n) for _, n, _, _ in meta["kn_tasks"]]
     assert sum(counts) == len(meta["kn_segs"]) and max(counts) == 2 and counts.count(2) == 512
-    assert p.layout.kn_rows == 8
+    assert p.layout.kn_class_ctas[1] > 0 and sum(p.layout.kn_class_ctas[c] for c in (0, 2, 3, 4)) == 0
     check_b200_arrays(p, 4)
     # mixed spans and rows never exceed a tile
-    items = [(h, 4 * (1 + (i % 2)), i, 1000 * i, 1 + (i * 37) % 200, i, -1) for i in range(60) for h in range(2)]
+    items = [(h, 4 * (1 + (i % 2)), i, 1000 * i, 1 + (i * 37) % 200, i, -1, 0) for i in range(60) for h in range(2)]
     for task in kernels.pack_segments(items):
         if len(task) > 1:
             assert sum(-(-it[4] // 32) * 32 for it in task) <= 128 and sum(it[1] for it in task) <= 16

@@ -19,8 +19,14 @@ bool layout_ok(const ta_plan_layout* L) {
     return false;
   if (L->num_small_tasks < 0 || L->num_tc_tasks < 0 || L->num_kn_tasks < 0 || L->kn_ctas < 0 || L->kstart_stride < 1)
     return false;
-  if (L->num_kn_tasks > 0 && (L->kn_ctas < 1 || L->kn_rows < 1 || L->kn_rows > 64 || L->num_kn_segs < 1)) return false;
-  if ((L->off_kn_tasks & 3) || (L->off_kn_segs & 3)) return false;   // int4 loads
+  int64_t class_ctas = 0;
+  for (int c = 0; c < 5; ++c) {
+    if (L->kn_class_ctas[c] < 0) return false;
+    class_ctas += L->kn_class_ctas[c];
+  }
+  if (class_ctas != L->kn_ctas) return false;
+  if (L->num_kn_tasks > 0 && (L->kn_ctas < 1 || L->num_kn_segs < 1)) return false;
+  if ((L->off_kn_tasks & 3) || (L->off_kn_segs & 3) || (L->off_tc_tasks & 3)) return false;   // int4 loads
   const int32_t* e = L->small_class_end;
   if (e[0] < 0 || e[1] < e[0] || e[2] < e[1] || e[2] != L->num_small_tasks) return false;
   return true;
@@ -63,7 +69,7 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
   if (tasks == 0) return TA_OK;
   if (!q || !kpool || !vpool || !part || !lse) return TA_ERR_ARG;
   // bulk copies and TMA need 16-byte aligned bases; rows are 2*head_dim bytes
-  if (!aligned16(q) || !aligned16(kpool) || !aligned16(vpool) || !aligned16(part)) return TA_ERR_ARG;
+  if (!aligned16(meta) || !aligned16(q) || !aligned16(kpool) || !aligned16(vpool) || !aligned16(part)) return TA_ERR_ARG;
   if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && head_dim != 128) return TA_ERR_UNSUPPORTED;
   // TMA coordinates are 32-bit
   if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && pool_tokens > int64_t(INT32_MAX) - 512) return TA_ERR_ARG;
@@ -104,7 +110,7 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err = cudaSuccess;
   if (plan->num_tc_tasks > 0) err = launch_seg_tc(p, plan->num_tc_tasks, dtype, s);
-  if (err == cudaSuccess && plan->num_kn_tasks > 0) err = launch_seg_kn(p, plan->kn_rows, dtype, s);
+  if (err == cudaSuccess && plan->num_kn_tasks > 0) err = launch_seg_kn(p, plan->kn_class_ctas, dtype, s);
   if (err == cudaSuccess && plan->num_small_tasks > 0)
     err = launch_seg_simt(p, plan->small_class_end, plan->small_max_keys, head_dim, dtype, s);
   return launch_status(err);

@@ -83,7 +83,7 @@ constexpr int kLook = 3;                    // S runs this many tiles ahead of P
 // task slot: int4 {nseg, ntiles, rows, flags}, then per segment three int4
 // {head, row0, rows, keys now} {first key of its slot, slot keys, job, k0}
 // {first partial row, first request (-1 unless the job's requests are
-// contiguous), 0, 0}.  Every role copies a slot into registers with vector
+// contiguous), first request index within the job, 0}.  Every role copies a slot into registers with vector
 // loads once per task (no shared-memory store in between), so no access to it
 // waits on another.
 constexpr int kSegWords = 12;
@@ -91,7 +91,7 @@ constexpr int kTaskWords = 4 + kSegMax * kSegWords;         // 52
 enum TaskFlag { TASK_BAD = 1, TASK_WRITE = 2 };
 
 struct SegR {
-  int head, row0, rows, nk, kt, span, job, k0, prow0, q0;
+  int head, row0, rows, nk, kt, span, job, k0, prow0, q0, qofs;
 };
 struct TaskR {
   int nseg, ntiles, rows, flags;
@@ -109,7 +109,7 @@ __device__ __forceinline__ TaskR load_task(const int* w) {
 #pragma unroll
   for (int s = 0; s < kSegMax; ++s) {
     const int4 a = v[1 + 3 * s], b = v[2 + 3 * s], c = v[3 + 3 * s];
-    t.seg[s] = SegR{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y};
+    t.seg[s] = SegR{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z};
   }
   return t;
 }
@@ -194,6 +194,8 @@ __device__ __forceinline__ void decode_task(const SegParams& p, int nseg, const 
     bad = true;
   }
   const int q0 = (c.x >= 0 && int64_t(c.x) + nreq <= p.num_requests) ? c.x : -1;
+  const int qofs = c.y;                            // the segment's first request within its job
+  ok = ok && qofs >= 0 && qofs + nreq <= p.max_requests;
   const bool all_ok = nseg >= 1 && nseg <= kSegMax && __all_sync(0xffffffffu, !mine || ok);
   const int rows = __shfl_sync(0xffffffffu, row0 + srows, (nseg - 1) & 31);
   const bool any = __any_sync(0xffffffffu, mine && nk > 0);
@@ -205,7 +207,7 @@ __device__ __forceinline__ void decode_task(const SegParams& p, int nseg, const 
     const bool keep = good && mine;
     v[1 + 3 * lane] = keep ? make_int4(head, row0, srows, nk) : make_int4(0, 0, 0, 0);
     v[2 + 3 * lane] = keep ? make_int4(kt, nseg == 1 ? kKeys : span, job, k0) : make_int4(0, 0, 0, 0);
-    v[3 + 3 * lane] = keep ? make_int4(prow0, q0, 0, 0) : make_int4(0, -1, 0, 0);
+    v[3 + 3 * lane] = keep ? make_int4(prow0, q0, qofs, 0) : make_int4(0, -1, 0, 0);
   }
   if (lane == 0) {
     v[0] = good ? make_int4(nseg, nseg == 1 ? (nk0 + kKeys - 1) / kKeys : (any ? 1 : 0), rows,
@@ -296,7 +298,8 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_trigger();             // the merge may be placed early; it waits for this kernel's completion
   const int G = p.group;
-  int begin = p.kn_offsets[blockIdx.x], end = p.kn_offsets[blockIdx.x + 1];
+  const int cta = p.kn_cta_base + int(blockIdx.x);
+  int begin = p.kn_offsets[cta], end = p.kn_offsets[cta + 1];
   if (begin < 0 || end < begin || end > p.num_kn_tasks) {
     if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
     begin = end = 0;
@@ -404,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
           if (x < t.nseg && r >= t.seg[x].row0) sg = t.seg[x];
         const int lr = r - sg.row0;
         const int req = int((uint32_t(lr) * p.gmul) >> 16);         // lr / G (lr < 64, G <= 64)
-        const int rid = sg.q0 >= 0 ? sg.q0 + req : p.qids[int64_t(sg.job) * p.max_requests + req];
+        const int rid = sg.q0 >= 0 ? sg.q0 + req : p.qids[int64_t(sg.job) * p.max_requests + sg.qofs + req];
         int64_t src_row = -1;
         if (rid >= 0 && rid < p.num_requests)
           src_row = (int64_t(rid) * p.num_q_heads + sg.head * G + (lr - req * G)) * kDim;
@@ -942,7 +945,7 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
 }
 
 template <typename T, int R>
-cudaError_t launch_r(const SegParams& p, cudaStream_t stream) {
+cudaError_t launch_r(const SegParams& p, int ctas, cudaStream_t stream) {
   CUtensorMap tk, tv;
   if (!make_pool_map(&tk, p.k, p.pool_tokens, p.num_kv_heads, kBoxRows) ||
       !make_pool_map(&tv, p.v, p.pool_tokens, p.num_kv_heads, kBoxRows))
@@ -954,27 +957,38 @@ cudaError_t launch_r(const SegParams& p, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     configured = true;
   }
-  cudaError_t err = launch_dependent(kernel, dim3(p.kn_ctas), dim3(kThreads), KnCfg<R>::alloc, stream, p, tk, tv);
+  cudaError_t err = launch_dependent(kernel, dim3(ctas), dim3(kThreads), KnCfg<R>::alloc, stream, p, tk, tv);
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 
+// One launch per non-empty row class, each over its own range of CTAs.
 template <typename T>
-cudaError_t launch_t(const SegParams& p, int rows, cudaStream_t stream) {
-  if (rows <= 4) return launch_r<T, 4>(p, stream);
-  if (rows <= 8) return launch_r<T, 8>(p, stream);
-  if (rows <= 16) return launch_r<T, 16>(p, stream);
-  if (rows <= 32) return launch_r<T, 32>(p, stream);
-  if (rows <= 64) return launch_r<T, 64>(p, stream);
-  return cudaErrorInvalidValue;
+cudaError_t launch_t(const SegParams& p, const int32_t class_ctas[5], cudaStream_t stream) {
+  SegParams q = p;
+  q.kn_cta_base = 0;
+  cudaError_t err = cudaSuccess;
+  for (int c = 0; c < 5 && err == cudaSuccess; ++c) {
+    const int n = class_ctas[c];
+    if (n <= 0) continue;
+    switch (c) {
+      case 0: err = launch_r<T, 4>(q, n, stream); break;
+      case 1: err = launch_r<T, 8>(q, n, stream); break;
+      case 2: err = launch_r<T, 16>(q, n, stream); break;
+      case 3: err = launch_r<T, 32>(q, n, stream); break;
+      default: err = launch_r<T, 64>(q, n, stream); break;
+    }
+    q.kn_cta_base += n;
+  }
+  return err;
 }
 
 }  // namespace
 
-cudaError_t launch_seg_kn(const SegParams& p, int rows, int dtype, cudaStream_t stream) {
+cudaError_t launch_seg_kn(const SegParams& p, const int32_t class_ctas[5], int dtype, cudaStream_t stream) {
   if (p.num_kn_tasks <= 0 || p.kn_ctas <= 0) return cudaSuccess;
-  if (dtype == TA_DTYPE_BF16) return launch_t<__nv_bfloat16>(p, rows, stream);
-  if (dtype == TA_DTYPE_F16) return launch_t<__half>(p, rows, stream);
+  if (dtype == TA_DTYPE_BF16) return launch_t<__nv_bfloat16>(p, class_ctas, stream);
+  if (dtype == TA_DTYPE_F16) return launch_t<__half>(p, class_ctas, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -142,8 +142,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int task = blockIdx.x, head = blockIdx.y;
   const int G = p.group;
 
-  const int piece = p.tc_tasks[2 * task];
-  const int pair = p.tc_tasks[2 * task + 1];
+  const int4 rec = reinterpret_cast<const int4*>(p.tc_tasks)[task];
+  const int piece = rec.x, pair = rec.y;
   Piece pc;
   const int state = resolve_piece(p, piece, pc);
   const int r0 = pair * 2 * kRows;
@@ -212,6 +212,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_prefetch_l2(map, 64, int(k0) + (j + kPrefetch) * kKeys, head);
         }
         if (j >= stages && !mbar_wait(&empty[st], ((j / stages) + 1) & 1, p.status)) break;
+        // the second stage waits until tile A's queries are in: the first
+        // tile's K and V and the queries share the start-up bandwidth alone
+        if (j == 1 && !mbar_wait(&bars[Q_FULL], 0, p.status)) break;
         const int y = int(k0) + j * kKeys;
         unsigned char* dst = ring + st * kTileBytes;
         mbar_arrive_expect_tx(&full[st], kTileBytes);
@@ -342,7 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint4* src = nullptr;
         if (trow < rows) {
           const int grow = r0 + trow;
-          const int rid = p.qids[int64_t(job) * p.max_requests + grow / G];
+          const int q0 = (rec.z >= 0 && int64_t(rec.z) + pc.nr <= p.num_requests) ? rec.z : -1;
+          const int rid = q0 >= 0 ? q0 + grow / G : p.qids[int64_t(job) * p.max_requests + grow / G];
           if (rid >= 0 && rid < p.num_requests)
             src = reinterpret_cast<const uint4*>(p.q + (int64_t(rid) * p.num_q_heads + head * G + grow % G) * kDim);
           else

@@ -19,7 +19,7 @@ struct SegParams {
   const int32_t* klen;       // [J]
   const int32_t* pieces;     // [P, 4] job, key offset, keys, first partial slot
   const int32_t* small_tasks;  // [n, 2] (piece, 16-row tile)
-  const int32_t* tc_tasks;     // [n, 2] (piece, 256-row pair)
+  const int32_t* tc_tasks;     // [n, 4] (piece, 256-row pair, first request if contiguous else -1, 0)
   const int32_t* kn_offsets;   // [kn_ctas + 1]
   const int32_t* kn_tasks;     // [n, 4] task headers
   const int32_t* kn_segs;      // [m, 8] segments
@@ -28,6 +28,7 @@ struct SegParams {
   int32_t num_jobs, num_pieces, max_requests, kstart_stride, num_requests, num_partials;
   int32_t num_q_heads, num_kv_heads, group;
   int32_t num_kn_tasks, num_kn_segs, kn_ctas;
+  int32_t kn_cta_base;         // first kn_offsets entry of the current keys-in-lanes launch
   float scale_log2;          // log2(e) / sqrt(D)
   uint32_t gmul;             // ceil(65536 / group): x / group == (x * gmul) >> 16 for x < 65536 / group
 };
@@ -86,7 +87,7 @@ struct MergeParams {
 cudaError_t launch_seg_simt(const SegParams& p, const int32_t class_end[3], int max_keys, int head_dim, int dtype,
                             cudaStream_t stream);
 cudaError_t launch_seg_tc(const SegParams& p, int num_tasks, int dtype, cudaStream_t stream);
-cudaError_t launch_seg_kn(const SegParams& p, int rows, int dtype, cudaStream_t stream);
+cudaError_t launch_seg_kn(const SegParams& p, const int32_t class_ctas[5], int dtype, cudaStream_t stream);
 cudaError_t launch_merge(const MergeParams& p, int head_dim, int dtype, cudaStream_t stream);
 cudaError_t launch_fill_klen(int32_t* klen, const int32_t* idx, int n, int value, int num_jobs, int32_t* status,
                              cudaStream_t stream);

@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libtree_attn_b200.so")
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 DTYPE_BF16 = 1
 DTYPE_F16 = 2
@@ -39,8 +39,8 @@ class PlanLayout(ctypes.Structure):
     """Mirror of ``ta_plan_layout``."""
     _fields_ = [(name, ctypes.c_int32) for name in (
         "num_jobs", "max_requests", "max_slots", "num_requests", "num_pieces", "num_partials", "max_pslots",
-        "num_small_tasks", "num_tc_tasks", "num_kn_tasks", "num_kn_segs", "kn_ctas", "kn_rows")]
-    _fields_ += [("small_class_end", ctypes.c_int32 * 3)]
+        "num_small_tasks", "num_tc_tasks", "num_kn_tasks", "num_kn_segs", "kn_ctas")]
+    _fields_ += [("kn_class_ctas", ctypes.c_int32 * 5), ("small_class_end", ctypes.c_int32 * 3)]
     _fields_ += [(name, ctypes.c_int32) for name in (
         "small_max_keys", "kstart_stride", "off_qids", "off_kstart", "off_qlen", "off_klen", "off_slots",
         "off_counts", "off_pieces", "off_pcounts", "off_cslots", "off_small_tasks", "off_tc_tasks",

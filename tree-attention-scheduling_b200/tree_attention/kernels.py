@@ -161,6 +161,17 @@ def split_pieces(jobs, groups, heads, use_tc, sms, no_split_from=None):
 # softmax chains interleave on every SM.
 KN_DUAL_ROWS = 8
 KN_DUAL_CTAS = 2
+# Query rows of one keys-in-lanes segment: larger jobs are cut into segments
+# of whole requests (each re-reads the job's K/V tiles, mostly from L2).
+KN_TASK_ROWS = 16
+# Row classes of the keys-in-lanes launches (the kernel's N dimension is
+# max(16, class rows)).
+KN_CLASS_ROWS = (4, 8, 16, 32, 64)
+
+
+def kn_class(rows):
+    """Row class of a keys-in-lanes task with `rows` query rows."""
+    return next(c for c, r in enumerate(KN_CLASS_ROWS) if rows <= r)
 KN_BOX = 32          # keys-in-lanes TMA box height: packed segments start on 32-key boundaries
 KN_PACK_ROWS = 16    # query rows of a packed tile
 KN_PACK_SEGS = 4     # segments of a packed tile
@@ -169,7 +180,8 @@ KN_PACK_SEGS = 4     # segments of a packed tile
 def pack_segments(items):
     """Group keys-in-lanes segments into tasks.
 
-    ``items`` are ``(head, rows, first_partial_row, k0, keys, job_flags, first_request)``.  A segment of more
+    ``items`` are ``(head, rows, first_partial_row, k0, keys, job_flags, first_request,
+    request_offset)``.  A segment of more
     than one 128-key tile is a task of its own; shorter ones are packed, best
     fit by their 32-key-rounded span, into tiles of 128 keys, at most
     KN_PACK_SEGS segments and KN_PACK_ROWS query rows each (a segment of more
@@ -289,41 +301,56 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
             reqs = jobs[i].requests
             q0 = reqs[0] if reqs[-1] - reqs[0] + 1 == len(reqs) else -1
             for h in range(heads):
-                items.append((h, rows[i], int(pieces[p, 3]) * groups, jobs[i].tokens[0] + offset, take, i | (growing << 30),
-                              q0))
+                # at most KN_TASK_ROWS rows per segment (whole requests): one
+                # launch class for nearly every plan, and short softmax chains
+                chunk = max(groups, KN_TASK_ROWS // groups * groups)
+                for r0 in range(0, rows[i], chunk):
+                    c0 = r0 // groups
+                    items.append((h, min(chunk, rows[i] - r0), int(pieces[p, 3]) * groups + r0,
+                                  jobs[i].tokens[0] + offset, take, i | (growing << 30),
+                                  q0 + c0 if q0 >= 0 else -1, c0))
         elif route[i] == "tc":
-            tc.extend((p, t) for t in range(ceil(rows[i] / TC_ROWS)))
+            reqs = jobs[i].requests
+            q0 = reqs[0] if reqs[-1] - reqs[0] + 1 == len(reqs) else -1
+            tc.extend((p, t, q0, 0) for t in range(ceil(rows[i] / TC_ROWS)))
         else:
             for t in range(ceil(rows[i] / SMALL_ROWS)):
                 small[_small_class(min(SMALL_ROWS, rows[i] - t * SMALL_ROWS))].append((p, t))
     class_end = np.cumsum([len(c) for c in small]).astype(np.int32)
     small_max_keys = max((piece_list[p][2] for c in small for p, _ in c), default=0)
     small_tasks = np.array([t for c in small for t in c], dtype=np.int32).reshape(-1, 2)
-    tc_tasks = np.array(tc, dtype=np.int32).reshape(-1, 2)
+    tc_tasks = np.array(tc, dtype=np.int32).reshape(-1, 4)
     tasks = pack_segments(items)
     segs = []
-    headers = []
-    costs = []
+    by_class = [[] for _ in KN_CLASS_ROWS]          # (header, cost) per row class
     for task in tasks:
-        headers.append((len(segs), len(task), 0, 0))
+        header = (len(segs), len(task), 0, 0)
         row0, kt = 0, 0
-        for h, r, first_row, k0, keys, job, q0 in task:
-            segs.append((h, row0, r, first_row, k0, kt if len(task) > 1 else 0, keys, job, q0, 0, 0, 0))
+        for h, r, first_row, k0, keys, job, q0, qofs in task:
+            segs.append((h, row0, r, first_row, k0, kt if len(task) > 1 else 0, keys, job, q0, qofs, 0, 0))
             row0 += r
             kt += -(-keys // KN_BOX) * KN_BOX
-        costs.append(_tiles(max(s[4] for s in task)) + 1)
-    kn_rows = max((sum(s[1] for s in task) for task in tasks), default=0)
-    kn_ctas = min(sms * (KN_DUAL_CTAS if kn_rows <= KN_DUAL_ROWS else 1), len(tasks))
-    if tasks:
-        kn_offsets, order = assign_lpt(costs, kn_ctas)
-        kn_tasks = np.array(headers, dtype=np.int32)[order]
-    else:
-        kn_offsets, kn_tasks = np.zeros(1, dtype=np.int32), np.zeros((0, 4), dtype=np.int32)
+        by_class[kn_class(row0)].append((header, _tiles(max(s[4] for s in task)) + 1))
+    # one launch per non-empty class, each balanced over its own CTAs
+    kn_class_ctas = np.zeros(len(KN_CLASS_ROWS), dtype=np.int32)
+    offsets, ordered = [0], []
+    for c, entries in enumerate(by_class):
+        if not entries:
+            continue
+        ctas = min(sms * (KN_DUAL_CTAS if KN_CLASS_ROWS[c] <= KN_DUAL_ROWS else 1), len(entries))
+        offs, order = assign_lpt([cost for _, cost in entries], ctas)
+        base = len(ordered)
+        offsets.extend(int(o) + base for o in offs[1:])
+        ordered.extend(entries[i][0] for i in order)
+        kn_class_ctas[c] = ctas
+    kn_ctas = int(kn_class_ctas.sum())
+    kn_offsets = np.array(offsets, dtype=np.int32)
+    kn_tasks = np.array(ordered, dtype=np.int32).reshape(-1, 4)
     kn_segs = np.array(segs, dtype=np.int32).reshape(-1, 12)
     return dict(qids=qids, kids=kids, qlen=qlen, klen=klen, slots=slots, counts=counts,
                 pieces=pieces, pcounts=pcounts, cslots=cslots, small_tasks=small_tasks, tc_tasks=tc_tasks,
                 kn_offsets=kn_offsets, kn_tasks=kn_tasks, kn_segs=kn_segs, small_class_end=class_end,
-                small_max_keys=small_max_keys, kn_ctas=kn_ctas, kn_rows=kn_rows, contiguous_k=contiguous_k,
+                small_max_keys=small_max_keys, kn_ctas=kn_ctas, kn_class_ctas=kn_class_ctas, contiguous_k=contiguous_k,
                 num_partials=slot)
 
 
@@ -391,7 +418,8 @@ def prepare(plan, q, num_kv_heads=None, _no_split_from=None):
     layout.num_kn_tasks = meta["kn_tasks"].shape[0]
     layout.num_kn_segs = meta["kn_segs"].shape[0]
     layout.kn_ctas = meta["kn_ctas"]
-    layout.kn_rows = meta["kn_rows"]
+    for c in range(len(KN_CLASS_ROWS)):
+        layout.kn_class_ctas[c] = int(meta["kn_class_ctas"][c])
     for i in range(3):
         layout.small_class_end[i] = int(meta["small_class_end"][i])
     layout.small_max_keys = meta["small_max_keys"]
