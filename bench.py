@@ -195,7 +195,7 @@ class Step:
         self.lib = _lib.load()
         L = prepared.layout
         self.launches = (sum(1 for i, e in enumerate(L.small_class_end) if e > (L.small_class_end[i - 1] if i else 0))
-                         + (1 if L.num_tc_tasks else 0) + (1 if L.num_kn_tasks else 0) + 1)
+                         + (1 if L.num_tc_tasks else 0) + sum(1 for c in range(5) if L.kn_class_ctas[c] > 0) + 1)
 
     def segment(self, copy=0):
         p = self.p
@@ -477,6 +477,41 @@ def run_grid(args):
     print(json.dumps(line), flush=True)
 
 
+def run_calibrate(args):
+    """Fit CostModel.b200()'s constants on the calibration grid (disjoint from the evaluation grid)."""
+    from tree_attention import calibration, workloads
+    import math
+    torch.cuda.set_device(0)
+    trees, inputs = [], []
+    for index, (params, tree) in enumerate(workloads.calibration_grid()):
+        copies = max(1, min(8, math.ceil((256 << 20) / kv_bytes(tree))))
+        trees.append(tree)
+        inputs.append(random_inputs(tree, len(tree.paths), "cuda", 501 + index, copies))
+    position = {id(t): i for i, t in enumerate(trees)}
+    steps, warmup = max(3, args.steps), max(3, args.warmup)
+
+    def measure(model, tree):
+        copies = inputs[position[id(tree)]]
+        prepared = kernels.prepare(schedule(tree, HQ, HK, D, "cube", model), copies[0][0])
+        step = Step(copies, prepared)
+        n = len(copies)
+        graph = capture(lambda: [(step.segment(i % n), step.merge(i % n)) for i in range(steps)])
+        us = time_graph(graph, steps, warmup, 1)
+        kernels.check_status(prepared)
+        del graph, step, prepared
+        return us
+
+    t0 = time.perf_counter()
+    best, score, history = calibration.fit(trees, measure, log=lambda h: print(json.dumps(h), file=sys.stderr,
+                                                                             flush=True))
+    start = history[0]["geomean_us"]
+    line = {"config": "calibrate: cost-model constants fitted on workloads.calibration_grid() (24 trees)",
+            "metric": "geomean decode-step time over the calibration trees (us)",
+            "start": start, "fitted": round(score, 3), "constants": best, "evaluated": len(history),
+            "seconds": round(time.perf_counter() - t0, 1), "steps": steps, "warmup": warmup}
+    print(json.dumps(line), flush=True)
+
+
 def run_decode(args):
     """a 32-request 2-level tree, 16 decode steps, plan reused vs rebuilt."""
     from tree_attention import workloads
@@ -563,7 +598,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--burn-s", type=float, default=1.0, help="sustained untimed load before timing (clocks)")
-    ap.add_argument("--config", choices=["headline", "grid", "decode"], default="headline")
+    ap.add_argument("--config", choices=["headline", "grid", "decode", "calibrate"], default="headline")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--quick", action="store_true",
                     help="main plan only: no burn, other plans, CPU baseline or repeated e2e (profiling runs)")
@@ -576,6 +611,8 @@ def main():
         run_grid(args)
     elif args.config == "decode":
         run_decode(args)
+    elif args.config == "calibrate":
+        run_calibrate(args)
     else:
         run_b200(args)
 

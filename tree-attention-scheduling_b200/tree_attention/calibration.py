@@ -1,7 +1,21 @@
-"""B200 re-calibration of the scheduler's cost model.
+"""B200 re-calibration of the scheduler's cost model (reference schedule.py:29-52).
 
-Initial constants; replaced by the fitted values once calibrated on the GPU.
+The reference's constants describe its Ascend kernels; ``CostModel.b200()``
+uses constants fitted to this package's sm_100a kernels.  ``fit`` searches
+them by coordinate descent: starting from ``start``, it tries every value of
+``SEARCH`` for one constant at a time, schedules every calibration tree with
+the candidate constants, measures the resulting decode step on the GPU
+(``measure(model, tree) -> microseconds``, supplied by the caller: ``bench.py
+--config calibrate``) and keeps a candidate whose geometric-mean step time over
+the trees is lower by more than ``min_gain``.  The calibration trees
+(``workloads.calibration_grid``) share no request count, shared fraction or
+branching factor with the evaluation grid the fitted model is judged on.
+
+``B200_CONSTANTS`` holds the result of the last fit (the command and its
+output are kept beside the measurements of this package).
 """
+import math
+from dataclasses import asdict
 
 B200_CONSTANTS = dict(
     bandwidth=6_000_000.0,
@@ -13,3 +27,61 @@ B200_CONSTANTS = dict(
     kv_split=1024,
     max_query_rows=512,
 )
+
+# Values tried for each constant, in this order.
+SEARCH = dict(
+    kv_split=(512, 1024, 2048, 4096),
+    max_query_rows=(64, 128, 256, 512, 1024),
+    task_us=(0.005, 0.02, 0.05, 0.1, 0.3),
+    merge_us=(0.0005, 0.002, 0.01, 0.03, 0.1),
+    bandwidth=(2_000_000.0, 4_000_000.0, 6_000_000.0, 9_000_000.0),
+    cube_flops=(300_000_000.0, 600_000_000.0, 1_200_000_000.0, 2_400_000_000.0),
+    cube_rows=(16, 32, 64),
+    key_tile=(128, 256),
+)
+
+
+def geomean(values):
+    return math.exp(sum(math.log(v) for v in values) / len(values))
+
+
+def fit(trees, measure, start=None, passes=2, min_gain=0.01, log=None):
+    """Coordinate descent of the cost-model constants on measured step times.
+
+    ``trees``: calibration trees; ``measure(model, tree)``: device microseconds
+    of one decode step of ``schedule(tree, ..., model)``.  Returns
+    ``(constants, geomean_us, history)`` where history lists every evaluated
+    candidate with its geometric-mean step time.
+    """
+    from .schedule import CostModel
+    best = dict(start or B200_CONSTANTS)
+    cache = {}
+    history = []
+
+    def score(consts):
+        key = tuple(sorted(consts.items()))
+        if key not in cache:
+            model = CostModel(**consts)
+            cache[key] = geomean([measure(model, tree) for tree in trees])
+            history.append(dict(consts, geomean_us=round(cache[key], 3)))
+            if log:
+                log(history[-1])
+        return cache[key]
+
+    best_score = score(best)
+    for _ in range(passes):
+        improved = False
+        for name, values in SEARCH.items():
+            for value in values:
+                candidate = dict(best, **{name: value})
+                s = score(candidate)
+                if s < best_score * (1.0 - min_gain):
+                    best, best_score, improved = candidate, s, True
+        if not improved:
+            break
+    return best, best_score, history
+
+
+def constants_of(model):
+    """The constants of a CostModel as a plain dict."""
+    return asdict(model)

@@ -163,7 +163,7 @@ KN_DUAL_ROWS = 8
 KN_DUAL_CTAS = 2
 # Query rows of one keys-in-lanes segment: larger jobs are cut into segments
 # of whole requests (each re-reads the job's K/V tiles, mostly from L2).
-KN_TASK_ROWS = 16
+KN_TASK_ROWS = 8
 # Row classes of the keys-in-lanes launches (the kernel's N dimension is
 # max(16, class rows)).
 KN_CLASS_ROWS = (4, 8, 16, 32, 64)
@@ -173,7 +173,7 @@ def kn_class(rows):
     """Row class of a keys-in-lanes task with `rows` query rows."""
     return next(c for c, r in enumerate(KN_CLASS_ROWS) if rows <= r)
 KN_BOX = 32          # keys-in-lanes TMA box height: packed segments start on 32-key boundaries
-KN_PACK_ROWS = 16    # query rows of a packed tile
+KN_PACK_ROWS = 8    # query rows of a packed tile
 KN_PACK_SEGS = 4     # segments of a packed tile
 
 
