@@ -171,10 +171,12 @@ def setup_dist(args):
 
 
 def max_over_ranks(value, world):
+    """The largest of every rank's `value` (device time of a multi-GPU step is the slowest rank's)."""
     if world == 1:
         return value
     import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    device = "cpu" if dist.get_backend() == "gloo" else "cuda"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 

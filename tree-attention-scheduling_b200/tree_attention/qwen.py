@@ -242,10 +242,11 @@ class SharedKVDecoder:
             vp.index_copy_(1, targets, v[:, :, 0, :].transpose(0, 1))
             result = attention_matrix(q[:, :, 0, :].contiguous(), kp, vp, prepared)
             if decoder.world > 1:
-                gathered = torch.empty((decoder.world, nreq, decoder.local_hq, decoder.dim), device=result.device,
+                # rank-major concatenation along dim 0 (the form every backend accepts)
+                gathered = torch.empty((decoder.world * nreq, decoder.local_hq, decoder.dim), device=result.device,
                                        dtype=result.dtype)
                 torch.distributed.all_gather_into_tensor(gathered, result.contiguous(), group=decoder.group)
-                result = gathered.permute(1, 0, 2, 3)
+                result = gathered.view(decoder.world, nreq, decoder.local_hq, decoder.dim).permute(1, 0, 2, 3)
             return module.o_proj(result.reshape(nreq, 1, -1)), None
 
         for layer in self.model.model.layers:
