@@ -131,7 +131,8 @@ __device__ __forceinline__ uint32_t swz_offset(int r, int c) {
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
-    seg_tc_kernel(SegParams p, const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v) {
+    seg_tc_kernel(SegParams p, const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                  const __grid_constant__ CUtensorMap tmap_q, int q_map_ok) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::off_bar);
@@ -160,6 +161,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t part_row0 = pc.slot * G + r0;
   const int ntiles = (nk + kKeys - 1) / kKeys;
   const int64_t head_rows = int64_t(head) * p.num_partials * G;
+  // The job's requests are consecutive: the query tiles come in by TMA
+  // (boxes of 128/G requests x G query heads), issued before the first K tile.
+  const int q0 = (rec.z >= 0 && int64_t(rec.z) + pc.nr <= p.num_requests) ? rec.z : -1;
+  const bool tma_q = q_map_ok && q0 >= 0;
 
   if (ntiles == 0) {  // empty segment: O = 0, LSE = -inf
     for (int i = tid; i < rows * kDim; i += kThreads) p.part[(head_rows + part_row0 + i / kDim) * kDim + i % kDim] = 0.f;
@@ -176,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars[S_FULL + s], 1);
       mbar_init(&bars[P_FULL + s], kSoftmaxWarps / 2);
       mbar_init(&bars[PV_DONE + s], 1);
-      mbar_init(&bars[Q_FULL + s], kSoftmaxWarps / 2);
+      mbar_init(&bars[Q_FULL + s], tma_q ? 1 : kSoftmaxWarps / 2);
     }
     mbar_init(&bars[V_TAIL], 1);
     fence_barrier_init();
@@ -201,6 +206,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       unsigned char* ring = smem + (is_k ? TcSmem::off_k : TcSmem::off_v);
       uint64_t* full = &bars[is_k ? K_FULL : V_FULL];
       uint64_t* empty = &bars[is_k ? K_EMPTY : V_EMPTY];
+      if (is_k && tma_q) {
+        for (int t = 0; t < ntile; ++t) {
+          unsigned char* qs = smem + TcSmem::off_q + t * kTileBytes;
+          const int z = q0 + (r0 + t * kRows) / G;
+          mbar_arrive_expect_tx(&bars[Q_FULL + t], kTileBytes);
+          tma_load_3d(qs, &tmap_q, 0, head * G, z, &bars[Q_FULL + t]);
+          tma_load_3d(qs + kHalfBytes, &tmap_q, 64, head * G, z, &bars[Q_FULL + t]);
+        }
+      }
       for (int j = 0; j < min(ntiles, kPrefetch); ++j) {
         tma_prefetch_l2(map, 0, int(k0) + j * kKeys, head);
         tma_prefetch_l2(map, 64, int(k0) + j * kKeys, head);
@@ -339,13 +353,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);
     const uint32_t s_col = kColS + t * kKeys, o_col = kColO + t * kDim;
     if (t < ntile) {
-      // this row of Q -> shared memory (K-major, 128B swizzle), zero for padding rows
-      {
+      // this row of Q -> shared memory (K-major, 128B swizzle), zero for padding
+      // rows, unless the producer brings the tile in by TMA
+      if (!tma_q) {
         unsigned char* qs = smem + TcSmem::off_q + t * kTileBytes;
         const uint4* src = nullptr;
         if (trow < rows) {
           const int grow = r0 + trow;
-          const int q0 = (rec.z >= 0 && int64_t(rec.z) + pc.nr <= p.num_requests) ? rec.z : -1;
           const int rid = q0 >= 0 ? q0 + grow / G : p.qids[int64_t(job) * p.max_requests + grow / G];
           if (rid >= 0 && rid < p.num_requests)
             src = reinterpret_cast<const uint4*>(p.q + (int64_t(rid) * p.num_q_heads + head * G + grow % G) * kDim);
@@ -357,10 +371,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 16; ++c) v[c] = src ? src[c] : make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4*>(qs + swz_offset(row, c)) = v[c];
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[Q_FULL + t]);
       }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[Q_FULL + t]);
 
       const float scale = p.scale_log2;
       float m_run = -INFINITY, z = 0.f;
@@ -484,10 +498,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <typename T>
 cudaError_t launch_typed(const SegParams& p, int num_tasks, cudaStream_t stream) {
-  CUtensorMap tk, tv;
+  CUtensorMap tk, tv, tq;
   if (!make_pool_map(&tk, p.k, p.pool_tokens, p.num_kv_heads, kKeys) ||
       !make_pool_map(&tv, p.v, p.pool_tokens, p.num_kv_heads, kKeys))
     return cudaErrorInvalidValue;
+  // query tiles by TMA when G divides the 128-row tile (else per-thread loads)
+  const int q_map_ok = make_query_map(&tq, p.q, p.num_requests, p.num_q_heads, p.group) ? 1 : 0;
+  if (!q_map_ok) tq = tk;
   auto kernel = seg_tc_kernel<T>;
   static bool configured = false;
   if (!configured) {
@@ -496,7 +513,7 @@ cudaError_t launch_typed(const SegParams& p, int num_tasks, cudaStream_t stream)
     configured = true;
   }
   dim3 grid(num_tasks, p.num_kv_heads);
-  kernel<<<grid, kThreads, TcSmem::alloc, stream>>>(p, tk, tv);
+  kernel<<<grid, kThreads, TcSmem::alloc, stream>>>(p, tk, tv, tq, q_map_ok);
   return cudaGetLastError();
 }
 

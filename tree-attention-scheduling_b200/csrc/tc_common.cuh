@@ -231,4 +231,21 @@ inline bool make_pool_map(CUtensorMap* map, const void* base, int64_t tokens, in
   return r == CUDA_SUCCESS;
 }
 
+// Queries [NREQ, HQ, 128] as a 3-D map (dim, query head, request) with boxes
+// of 64 dims x G heads x 128/G requests: one box is the 64-column half of a
+// 128-row query tile whose rows are (request, GQA row) pairs of consecutive
+// requests, laid out with the 128-byte swizzle like the K tiles.
+inline bool make_query_map(CUtensorMap* map, const void* q, int64_t requests, int q_heads, int group) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || requests <= 0 || q_heads <= 0 || group <= 0 || 128 % group || group > q_heads) return false;
+  cuuint64_t dims[3] = {128, cuuint64_t(q_heads), cuuint64_t(requests)};
+  cuuint64_t strides[2] = {128 * 2, cuuint64_t(q_heads) * 128 * 2};
+  cuuint32_t box[3] = {64, cuuint32_t(group), cuuint32_t(128 / group)};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(q), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace ta
