@@ -2,9 +2,9 @@
 // kernels.py:58-83), plus the tiny device update of a reused decode plan.
 //
 // One warp per (request, query head).  Instead of the reference's serial
-// running-max loop, lane k first loads the LSE of partial k so the maximum and
-// the weights come from two warp reductions; the partial rows are then read
-// with independent 16-byte loads (lanes split head_dim).
+// running-max loop, lane k loads the LSE of partial k so the maximum and the
+// weights come from two warp reductions; the partial rows are then read with
+// independent 16-byte loads (lanes split head_dim), eight rows in flight.
 #include "ta_common.cuh"
 #include "ta_kernels.cuh"
 
@@ -24,81 +24,76 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) 
   const int request = item / p.num_q_heads, head = item % p.num_q_heads;
   const int G = p.group, kv_head = head / G, g = head % G;
 
+  // The slot list is loaded together with the count (slot loads past the
+  // count are discarded), so the chain is count+slots -> LSEs -> rows.
+  const int32_t* slots = p.cslots + int64_t(request) * p.max_slots;
   int count = p.counts[request];
+  const int pre_slot = lane < p.max_slots ? slots[lane] : -1;
   if (count < 0 || count > p.max_slots) {
     if (lane == 0) set_status(p.status, TA_ERR_BOUNDS);
     count = 0;
   }
-  const int32_t* slots = p.cslots + int64_t(request) * p.max_slots;
   const int64_t head_rows = int64_t(kv_head) * p.num_partials;
 
-  auto row_of = [&](int k, bool& ok) -> int64_t {
-    const int s = slots[k];
-    ok = s >= 0 && s < p.num_partials;
-    return (head_rows + (ok ? s : 0)) * G + g;
-  };
-
-  // pass 1: maximum LSE over the request's partials
-  float m = -INFINITY;
-  for (int k0 = 0; k0 < count; k0 += 32) {
-    float l = -INFINITY;
-    if (k0 + lane < count) {
-      bool ok;
-      const int64_t row = row_of(k0 + lane, ok);
-      if (ok) l = p.lse[row];
-      else set_status(p.status, TA_ERR_BOUNDS);
-    }
-    m = fmaxf(m, warp_max(l));
-  }
-
-  // pass 2: weights exp(lse - m) and the weighted sum of partial rows; lane k
-  // owns the weight and row offset of partial k0 + k, and the rows are read
-  // four at a time so their loads overlap.
   float acc[DL];
 #pragma unroll
   for (int e = 0; e < DL; ++e) acc[e] = 0.f;
-  float z = 0.f;
-  if (m != -INFINITY) {
-    for (int k0 = 0; k0 < count; k0 += 32) {
-      float w = 0.f;
-      int64_t row = 0;
-      if (k0 + lane < count) {
-        bool ok;
-        row = row_of(k0 + lane, ok);
-        if (ok) w = fast_exp2((p.lse[row] - m) * kLog2e);  // -inf lse gives 0
+  float m = -INFINITY, z = 0.f;
+  // Lane k holds partial k0 + k of each group of 32: its LSE, weight and row.
+  // Groups after the first (more than 32 partials) rescale the running sums.
+  for (int k0 = 0; k0 < count; k0 += 32) {
+    const int k = k0 + lane;
+    float l = -INFINITY;
+    int64_t row = 0;
+    if (k < count) {
+      const int s = k0 == 0 ? pre_slot : slots[k];
+      if (s >= 0 && s < p.num_partials) {
+        row = (head_rows + s) * G + g;
+        l = p.lse[row];
+      } else {
+        set_status(p.status, TA_ERR_BOUNDS);
       }
-      z += warp_sum(w);
-      const int n = min(32, count - k0);
-      for (int j = 0; j < n; j += 4) {
-        float wj[4];
-        float x[4][DL];
+    }
+    const float m_new = fmaxf(m, warp_max(l));
+    if (m_new == -INFINITY) continue;               // nothing but empty partials so far
+    const float scale = fast_exp2((m - m_new) * kLog2e);   // m = -inf gives 0
+    z *= scale;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int src = min(j + u, n - 1);
-          wj[u] = __shfl_sync(0xffffffffu, w, src);
-          const int64_t rj = __shfl_sync(0xffffffffu, row, src);
-          if (j + u >= n) wj[u] = 0.f;
-          // an empty partial (weight 0) may hold anything: do not read it
-          const float* ptr = p.part + rj * D + lane * DL;
+    for (int e = 0; e < DL; ++e) acc[e] *= scale;
+    m = m_new;
+    const float w = fast_exp2((l - m) * kLog2e);        // -inf lse gives 0
+    z += warp_sum(w);
+    // every row of the group in flight at once (eight at a time)
+    const int n = min(32, count - k0);
+    for (int j = 0; j < n; j += 8) {
+      float wj[8];
+      float x[8][DL];
 #pragma unroll
-          for (int e = 0; e < DL; ++e) x[u][e] = 0.f;
-          if (wj[u] != 0.f) {
-            if constexpr (DL == 4) {
-              const float4 v = *reinterpret_cast<const float4*>(ptr);
-              x[u][0] = v.x; x[u][1] = v.y; x[u][2] = v.z; x[u][3] = v.w;
-            } else if constexpr (DL == 2) {
-              const float2 v = *reinterpret_cast<const float2*>(ptr);
-              x[u][0] = v.x; x[u][1] = v.y;
-            } else {
-              x[u][0] = ptr[0];
-            }
+      for (int u = 0; u < 8; ++u) {
+        const int src = min(j + u, n - 1);
+        wj[u] = __shfl_sync(0xffffffffu, w, src);
+        const int64_t rj = __shfl_sync(0xffffffffu, row, src);
+        if (j + u >= n) wj[u] = 0.f;
+        // an empty partial (weight 0) may hold anything: do not read it
+        const float* ptr = p.part + rj * D + lane * DL;
+#pragma unroll
+        for (int e = 0; e < DL; ++e) x[u][e] = 0.f;
+        if (wj[u] != 0.f) {
+          if constexpr (DL == 4) {
+            const float4 v = *reinterpret_cast<const float4*>(ptr);
+            x[u][0] = v.x; x[u][1] = v.y; x[u][2] = v.z; x[u][3] = v.w;
+          } else if constexpr (DL == 2) {
+            const float2 v = *reinterpret_cast<const float2*>(ptr);
+            x[u][0] = v.x; x[u][1] = v.y;
+          } else {
+            x[u][0] = ptr[0];
           }
         }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-          for (int e = 0; e < DL; ++e) acc[e] = fmaf(wj[u], x[u][e], acc[e]);
       }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int e = 0; e < DL; ++e) acc[e] = fmaf(wj[u], x[u][e], acc[e]);
     }
   }
   const float inv = z > 0.f ? 1.f / z : 0.f;
