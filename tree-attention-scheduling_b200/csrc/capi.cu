@@ -110,6 +110,7 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err = cudaSuccess;
   if (plan->num_tc_tasks > 0) err = launch_seg_tc(p, plan->num_tc_tasks, dtype, s);
+  p.kn_after_tc = plan->num_tc_tasks > 0 && err == cudaSuccess;
   if (err == cudaSuccess && plan->num_kn_tasks > 0) err = launch_seg_kn(p, plan->kn_class_ctas, dtype, s);
   if (err == cudaSuccess && plan->num_small_tasks > 0)
     err = launch_seg_simt(p, plan->small_class_end, plan->small_max_keys, head_dim, dtype, s);

@@ -18,6 +18,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) {
   constexpr int DL = D / 32;
   pdl_wait();                // the segment kernels before this one have completed
+  pdl_trigger();             // the next step's query-tile kernel may set up meanwhile (it waits before any data)
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
   if (item >= p.num_requests * p.num_q_heads) return;

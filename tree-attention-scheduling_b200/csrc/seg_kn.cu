@@ -296,7 +296,12 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::off_tmem);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  pdl_trigger();             // the merge may be placed early; it waits for this kernel's completion
+  // Placed early after the query-tile kernel of the same call (which places
+  // it only once the previous step's kernels are complete); after anything
+  // else, wait for it first.  Then the next launch (another row class or the
+  // merge, which waits for completion before reading) may be placed.
+  if (!p.kn_after_tc) pdl_wait();
+  pdl_trigger();
   const int G = p.group;
   const int cta = p.kn_cta_base + int(blockIdx.x);
   int begin = p.kn_offsets[cta], end = p.kn_offsets[cta + 1];

@@ -139,7 +139,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::off_tmem);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  pdl_trigger();             // the keys-in-lanes kernel may start on SMs this grid leaves free
   const int task = blockIdx.x, head = blockIdx.y;
   const int G = p.group;
 
@@ -150,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int r0 = pair * 2 * kRows;
   const int rows = state == PIECE_SKIP ? 0 : min(2 * kRows, pc.nr * G - r0);   // rows of this pair
   if (rows <= 0) {
+    pdl_wait();
     if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
     return;
   }
@@ -167,6 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool tma_q = q_map_ok && q0 >= 0;
 
   if (ntiles == 0) {  // empty segment: O = 0, LSE = -inf
+    pdl_wait();
     for (int i = tid; i < rows * kDim; i += kThreads) p.part[(head_rows + part_row0 + i / kDim) * kDim + i % kDim] = 0.f;
     for (int i = tid; i < rows; i += kThreads) p.lse[head_rows + part_row0 + i] = -INFINITY;
     return;
@@ -196,6 +197,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool alive = true;
+  // This kernel may have been placed while the kernel before it (the previous
+  // step's merge) still runs; everything above read only this launch's plan
+  // records.  Queries, pools and partial outputs wait for its completion, and
+  // only then may the keys-in-lanes kernel be placed (it writes partials too).
+  // Every CTA, early exits included, waits before it triggers or exits.
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0 || warp == kVProducerWarp) {
     // ---------------- TMA producers (K ring / V ring) ----------------
@@ -513,7 +521,8 @@ cudaError_t launch_typed(const SegParams& p, int num_tasks, cudaStream_t stream)
     configured = true;
   }
   dim3 grid(num_tasks, p.num_kv_heads);
-  kernel<<<grid, kThreads, TcSmem::alloc, stream>>>(p, tk, tv, tq, q_map_ok);
+  cudaError_t err = launch_dependent(kernel, grid, dim3(kThreads), TcSmem::alloc, stream, p, tk, tv, tq, q_map_ok);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

@@ -29,6 +29,7 @@ struct SegParams {
   int32_t num_q_heads, num_kv_heads, group;
   int32_t num_kn_tasks, num_kn_segs, kn_ctas;
   int32_t kn_cta_base;         // first kn_offsets entry of the current keys-in-lanes launch
+  int32_t kn_after_tc;         // the keys-in-lanes launches follow a query-tile launch of the same call
   float scale_log2;          // log2(e) / sqrt(D)
   uint32_t gmul;             // ceil(65536 / group): x / group == (x * gmul) >> 16 for x < 65536 / group
 };
