@@ -112,3 +112,28 @@ def test_decoder_matches_full_forward_gpu(shape, cached):
             torch.cuda.synchronize()
             reference = reference_logits(model, decoder.sequences)
             torch.testing.assert_close(logits.float(), reference.float(), atol=4e-3, rtol=2e-2)
+
+
+@pytest.mark.gpu
+def test_cached_decoder_graph_generate_gpu():
+    """The whole greedy decode step captured once as a CUDA graph (device-side argmax, KV append, tail
+    lengths): the final logits match full-sequence forwards of the generated sequences, and the tokens
+    are those the eager step loop picks."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    model = tiny_model(128, 8, 2, torch.float16, "cuda")
+    sequences = [s * 6 for s in SEQUENCES]
+    eager = qwen.CachedPrefixDecoder(model, sequences, max_new_tokens=6, method="cube", cost_model=CostModel.b200())
+    graphed = qwen.CachedPrefixDecoder(model, sequences, max_new_tokens=6, method="cube", cost_model=CostModel.b200())
+    for _ in range(4):
+        eager.step(eager.logits.argmax(-1).tolist())
+    tokens = graphed.generate(4)
+    assert len(tokens) == 4 and graphed.generated == 4 and graphed.used == eager.used
+    assert graphed.sequences == eager.sequences
+    torch.testing.assert_close(graphed.logits.float(), eager.logits.float(), atol=4e-3, rtol=2e-2)
+    reference = reference_logits(model, graphed.sequences)
+    torch.testing.assert_close(graphed.logits.float(), reference.float(), atol=4e-3, rtol=2e-2)
+    # continue eagerly after the graph: the plan's tail lengths and pools are consistent
+    graphed.step(graphed.logits.argmax(-1).tolist())
+    torch.testing.assert_close(graphed.logits.float(), reference_logits(model, graphed.sequences).float(),
+                               atol=4e-3, rtol=2e-2)

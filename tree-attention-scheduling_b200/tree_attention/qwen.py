@@ -207,17 +207,11 @@ class SharedKVDecoder:
         self.used += len(token_ids)
         return positions
 
-    @torch.inference_mode()
-    def step(self, token_ids):
-        """Feed one token per request; returns next-token logits ``[NREQ, vocab]``."""
-        token_ids = list(token_ids)
-        if len(token_ids) != len(self.sequences):
-            raise ValueError("one token per request")
-        positions = torch.tensor([[len(s)] for s in self.sequences], device=self.device)
-        targets = torch.tensor(self._append(token_ids), device=self.device)
-        prepared = self._prepare_plan()
+    def _attention_forward(self, prepared, targets, nreq):
+        """The decode-step attention of every layer: q/k/v projections (this rank's heads), q/k RMSNorm,
+        RoPE, append of the new K/V at ``targets`` (a device tensor of pool positions), tree attention
+        through ``attention_matrix`` and, when sharded, an all-gather of the heads before ``o_proj``."""
         pools, slices, decoder = self.pools, self._slices, self
-        nreq = len(token_ids)
 
         def forward(module, hidden_states, position_embeddings, attention_mask=None, **kwargs):
             shape = (*hidden_states.shape[:-1], -1, module.head_dim)
@@ -249,6 +243,18 @@ class SharedKVDecoder:
                 result = gathered.view(decoder.world, nreq, decoder.local_hq, decoder.dim).permute(1, 0, 2, 3)
             return module.o_proj(result.reshape(nreq, 1, -1)), None
 
+        return forward
+
+    @torch.inference_mode()
+    def step(self, token_ids):
+        """Feed one token per request; returns next-token logits ``[NREQ, vocab]``."""
+        token_ids = list(token_ids)
+        if len(token_ids) != len(self.sequences):
+            raise ValueError("one token per request")
+        positions = torch.tensor([[len(s)] for s in self.sequences], device=self.device)
+        targets = torch.tensor(self._append(token_ids), device=self.device)
+        prepared = self._prepare_plan()
+        forward = self._attention_forward(prepared, targets, len(token_ids))
         for layer in self.model.model.layers:
             layer.self_attn.forward = MethodType(forward, layer.self_attn)
         try:
@@ -282,3 +288,74 @@ class CachedPrefixDecoder(SharedKVDecoder):
 
     def _prepare_plan(self):
         return self.cached_plan.update(self.generated)
+
+    @torch.inference_mode()
+    def generate(self, steps):
+        """Greedy decode of ``steps`` tokens per request, the whole step recorded once as a CUDA graph.
+
+        One replay feeds every request the argmax of its previous logits
+        (computed on the device), appends the new K/V rows at the tails, sets
+        the tails' lengths in the plan on the device and runs the model: no
+        host round trip between steps.  Afterwards ``sequences``, ``logits``,
+        ``generated`` and ``used`` are as ``steps`` calls of
+        ``step(logits.argmax(-1))`` leave them.  Returns the generated tokens
+        ``[steps][NREQ]``.
+        """
+        if steps <= 0:
+            return []
+        if self.generated + steps > self.max_new_tokens:
+            raise ValueError("Decode exceeds allocated max_new_tokens")
+        nreq, dev, t0 = len(self.sequences), self.device, self.generated
+        t = torch.full((1,), t0, dtype=torch.int64, device=dev)            # tokens generated so far
+        start_pos = torch.tensor([len(s) for s in self.sequences], dtype=torch.int64, device=dev)
+        tail = torch.tensor([self.prefix_size + r * self.max_new_tokens for r in range(nreq)], dtype=torch.int64,
+                            device=dev)
+        first = self.logits.argmax(-1)
+        tokens = first.clone()
+        out = torch.zeros((steps, nreq), dtype=torch.int64, device=dev)
+        positions = torch.empty((nreq, 1), dtype=torch.int64, device=dev)
+        targets = torch.empty(nreq, dtype=torch.int64, device=dev)
+        tail_idx = self.cached_plan.tail_indices.long()
+        klen = self.cached_plan.prepared.klen
+        forward = self._attention_forward(self.cached_plan.prepared, targets, nreq)
+
+        def body():
+            positions.copy_((start_pos + (t - t0))[:, None])
+            targets.copy_(tail + t)
+            klen.index_copy_(0, tail_idx, (t + 1).to(torch.int32).expand(tail_idx.numel()))
+            out.index_copy_(0, (t - t0).clamp(max=steps - 1), tokens[None])
+            # a prepared (empty) mask mapping: the patched attention needs no mask, and building one
+            # would copy a host scalar, which a graph capture cannot record
+            logits = self.model(tokens[:, None], position_ids=positions, use_cache=False,
+                                attention_mask={"full_attention": None, "sliding_attention": None}).logits[:, 0]
+            tokens.copy_(logits.argmax(-1))
+            t.add_(1)
+            return logits
+
+        for layer in self.model.model.layers:
+            layer.self_attn.forward = MethodType(forward, layer.self_attn)
+        try:
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                body()                                   # warm-up (lazy library setup); its writes are redone
+            torch.cuda.current_stream(dev).wait_stream(side)
+            t.fill_(t0)
+            tokens.copy_(first)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                logits = body()
+            for _ in range(steps):
+                graph.replay()
+            generated = out.tolist()
+            self.logits = logits.clone()
+            del graph
+        finally:
+            for layer, original in zip(self.model.model.layers, self.original):
+                layer.self_attn.forward = original
+        for row in generated:
+            for sequence, token in zip(self.sequences, row):
+                sequence.append(token)
+        self.generated += steps
+        self.used += steps * nreq
+        return generated
