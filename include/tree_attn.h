@@ -101,7 +101,9 @@ typedef struct ta_plan_layout {
   /* keys-in-lanes tasks are grouped by query rows into classes of at most 4,
      8, 16, 32 and 64 rows, one launch per non-empty class; class c has
      kn_class_ctas[c] persistent CTAs, whose kn_offsets entries follow those
-     of the classes before it (the sum is kn_ctas) */
+     of the classes before it (the sum is kn_ctas).  This build has kernels
+     for the 4- and 8-row classes; a plan with CTAs in the others is rejected
+     with TA_ERR_UNSUPPORTED. */
   int32_t kn_class_ctas[5];
   /* small tasks are sorted by padded row count: [0, e0) need 4 rows,
      [e0, e1) 8 rows, [e1, e2) 16 rows; e2 == num_small_tasks */

@@ -184,14 +184,14 @@ def test_prepare_rejects_bad_plans():
 
 
 def test_pieces_split_long_jobs_and_keep_tails_whole():
-    # one job of 16 requests (64 rows) over 8192 keys: keys-in-lanes, cut into pieces
-    tree = KVTree.synthetic([-1] + [0] * 16, [8192] + [32] * 16, list(range(1, 17)))
+    # one job of 4 requests (16 rows) over 8192 keys: keys-in-lanes, cut into pieces
+    tree = KVTree.synthetic([-1] + [0] * 4, [8192] + [32] * 4, list(range(1, 5)))
     plan = schedule(tree, method="fixed", model=CostModel(kv_split=1 << 20, max_query_rows=4096))
-    q = torch.empty(16, 32, 128, dtype=torch.bfloat16)
+    q = torch.empty(4, 32, 128, dtype=torch.bfloat16)
     p = kernels.prepare(plan, q)
     meta = p.host_arrays
-    assert sum(1 for j in p.jobs if len(j.requests) == 16) == 1
-    root = [pc for pc in meta["pieces"] if meta["qlen"][pc[0]] == 16]
+    assert sum(1 for j in p.jobs if len(j.requests) == 4) == 1
+    root = [pc for pc in meta["pieces"] if meta["qlen"][pc[0]] == 4]
     assert len(root) > 1 and sum(int(pc[2]) for pc in root) == 8192
     assert all(pc[2] % kernels.KEY_TILE == 0 for pc in root[:-1])
     chunk = kernels.KN_TASK_ROWS
@@ -199,7 +199,7 @@ def test_pieces_split_long_jobs_and_keep_tails_whole():
     check_b200_arrays(p, 4)
     # decode tails (positions past the prompt) are never split and follow klen
     tails = [kernels.Job((r,), tuple(range(tree.storage_tokens + r * 4096, tree.storage_tokens + (r + 1) * 4096)))
-             for r in range(16)]
+             for r in range(4)]
     p2 = kernels.prepare(kernels.Plan(plan.jobs + tails, plan.method, plan.estimated_us, plan.settings), q,
                          _no_split_from=tree.storage_tokens)
     m2 = p2.host_arrays

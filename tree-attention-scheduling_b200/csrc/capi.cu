@@ -71,6 +71,8 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
   // bulk copies and TMA need 16-byte aligned bases; rows are 2*head_dim bytes
   if (!aligned16(meta) || !aligned16(q) || !aligned16(kpool) || !aligned16(vpool) || !aligned16(part)) return TA_ERR_ARG;
   if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && head_dim != 128) return TA_ERR_UNSUPPORTED;
+  // keys-in-lanes kernels are built for tasks of up to 8 query rows
+  if (plan->kn_class_ctas[2] > 0 || plan->kn_class_ctas[3] > 0 || plan->kn_class_ctas[4] > 0) return TA_ERR_UNSUPPORTED;
   // TMA coordinates are 32-bit
   if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && pool_tokens > int64_t(INT32_MAX) - 512) return TA_ERR_ARG;
 

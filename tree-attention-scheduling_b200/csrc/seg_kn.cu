@@ -976,12 +976,10 @@ cudaError_t launch_t(const SegParams& p, const int32_t class_ctas[5], cudaStream
   for (int c = 0; c < 5 && err == cudaSuccess; ++c) {
     const int n = class_ctas[c];
     if (n <= 0) continue;
-    switch (c) {
+    switch (c) {                  // the host builds tasks of at most 8 rows (classes 16-64 are rejected)
       case 0: err = launch_r<T, 4>(q, n, stream); break;
       case 1: err = launch_r<T, 8>(q, n, stream); break;
-      case 2: err = launch_r<T, 16>(q, n, stream); break;
-      case 3: err = launch_r<T, 32>(q, n, stream); break;
-      default: err = launch_r<T, 64>(q, n, stream); break;
+      default: err = cudaErrorInvalidValue; break;
     }
     q.kn_cta_base += n;
   }
