@@ -392,14 +392,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         float s[kKeys];
         {
-          uint32_t a[32];
+          uint32_t a[4][32];                  // four loads in flight, one wait
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            tmem_ld32(lane_addr + s_col + c * 32, a);
-            tmem_wait_ld();
+          for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + s_col + c * 32, a[c]);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(a[i]);
-          }
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(a[c][i]);
         }
         if (valid < kKeys) {
 #pragma unroll
@@ -468,11 +468,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv = (alive && z > 0.f) ? 1.f / z : 0.f;
       float* dst = p.part + (head_rows + part_row0 + trow) * kDim;
       const bool part32 = (reinterpret_cast<uintptr_t>(p.part) & 31u) == 0;   // rows are 512 bytes
+      uint32_t oa[4][32];                     // the whole O row: four loads in flight, one wait
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + o_col + c * 32, oa[c]);
+      tmem_wait_ld();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        tmem_ld32(lane_addr + o_col + c * 32, o);
-        tmem_wait_ld();
+        const uint32_t (&o)[32] = oa[c];
         if (trow < rows) {
           if (part32) {
 #pragma unroll
