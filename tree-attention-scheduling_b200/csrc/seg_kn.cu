@@ -37,13 +37,17 @@
 //   warps 0-3  softmax (thread = key = TMEM lane) and the per-task epilogue
 //              (thread = head dim = TMEM lane of O^T), deferred until after
 //              the next task's first tile so its P.V has time to finish
-//   warp 4     K producer (ring of STAGES 32 KB tiles)
-//   warp 5     V producer
-//   warp 6     MMA issue (lane 0): waits, zeroes V rows where needed, issues
-//              P.V(g), then S(g+3)
-//   warp 7     scheduler: task slots (decode + checks) and Q^T gathers into
-//              two buffers, each released by the MMA's commit after the last S
-//              of its previous task
+//   warp 4     K producer (ring of STAGES 32 KB tiles; loads carry an
+//              evict-first L2 hint: segment K/V is read once, and the step's
+//              partial outputs should stay in L2 for the merge)
+//   warp 5     V producer, likewise
+//   warp 6     MMA issue (lane 0): polls its inputs and issues S(g) up to
+//              kLook tiles ahead of P.V, and P.V(g) as soon as P(g) is
+//              written, zeroing V rows where needed
+//   warp 7     scheduler: task slots (warp-parallel decode + checks) and Q^T
+//              gathers (cp.async, published one task later) into kQBufs
+//              buffers, each released by the MMA's commit after the last S of
+//              its previous task
 //
 // Ordering facts the barrier scheme relies on: MMAs issued by one thread run in
 // issue order, and the issue order is S(0) S(1) S(2) PV(0) S(3) PV(1) S(4) ...
@@ -447,6 +451,7 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
       unsigned char* ring = smem + (is_k ? C::off_k : C::off_v);
       uint64_t* full = is_k ? k_full : v_full;
       uint64_t* empty = is_k ? k_empty : v_empty;
+      const uint64_t policy = l2_evict_first_policy();   // segment K/V is read once
       int g = 0;
       bool alive = true;
       for (int k = 0; k < count && alive; ++k) {
@@ -473,8 +478,8 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
 #pragma unroll 1
             for (int b = 0; b * kBoxRows < keys; ++b) {
               const uint32_t row = uint32_t(sg.kt + b * kBoxRows) * 128u;
-              tma_load_3d(dst + row, map, 0, y + b * kBoxRows, sg.head, &full[st]);
-              tma_load_3d(dst + kHalfBytes + row, map, 64, y + b * kBoxRows, sg.head, &full[st]);
+              tma_load_3d_hint(dst + row, map, 0, y + b * kBoxRows, sg.head, &full[st], policy);
+              tma_load_3d_hint(dst + kHalfBytes + row, map, 64, y + b * kBoxRows, sg.head, &full[st], policy);
             }
           }
         }
