@@ -1,12 +1,14 @@
-// Segment attention for small query groups (<= 64 rows per piece x KV head) on
-// the 5th-generation tensor cores, with the keys in the TMEM lanes.
+// Segment attention for small query groups (<= 16 rows per job x KV head, cut
+// into tasks of <= 8 rows) on the 5th-generation tensor cores, with the keys in
+// the TMEM lanes.
 //
 // A decode-time job shared by a few requests has few query rows (requests x
 // GQA group, e.g. 4 for a private leaf) and many keys.  Putting the keys on the
 // MMA's M side and the queries on N makes such a job a thin tcgen05 problem:
 //   S^T [128 keys x N] = K_tile [128 x 128 dims] . Q^T          (kind::f16, both K-major)
 //   O^T [128 dims x N] += V_tile^T [128 dims x 128 keys] . P^T  (A = V MN-major, B = P K-major)
-// with N = max(16, R) for a row class R in {4, 8, 16, 32, 64}; only R rows are
+// with N = max(16, R) for a row class R (the library instantiates R = 4 and 8;
+// the template is written for up to 64); only R rows are
 // touched on the CUDA cores.  Each thread of the softmax warps owns one key of
 // the tile (one TMEM lane), so scores need no cross-lane reduction; row sums
 // are kept per thread and reduced once per task.  Row maxima are handled with
@@ -23,7 +25,7 @@
 // of its own segment.  Packing turns the many one-tile private leaves of a
 // decode tree into full tiles, so their fixed per-tile costs are shared.
 //
-// The kernel is persistent: one CTA per SM walks a host-built list of tasks
+// The kernel is persistent: each CTA (two per SM for R <= 8) walks a host-built list of tasks
 // (longest-processing-time balanced).  A scheduler warp decodes and checks
 // each task ONCE into a ring of shared-memory task slots and gathers its Q^T
 // rows, running ahead of every other role; the K and V TMA producers run ahead
@@ -50,8 +52,8 @@
 //              its previous task
 //
 // Ordering facts the barrier scheme relies on: MMAs issued by one thread run in
-// issue order, and the issue order is S(0) S(1) S(2) PV(0) S(3) PV(1) S(4) ...
-// (S three tiles ahead), so observing S(g) complete implies PV(g-3) has
+// issue order, and S(g) is issued only once P.V(g-3) has been issued (S runs
+// at most three tiles ahead), so observing S(g) complete implies PV(g-3) has
 // completed, and P^T(g) is rewritten (as P^T(g+3)) only after S(g+3), issued
 // after PV(g).  A parity wait is only correct while its barrier is at most one
 // phase behind, so every per-tile barrier exists three times, by tile index
