@@ -810,7 +810,14 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
         // One barrier in the common case: the OR of "a wait was lost" and "a
         // row needs a new maximum"; a second one tells the two apart.
         bool rescale = false;
-        if (named_sync_or(1, kSoftmaxThreads, need || !ok)) {
+        if (j == 0) {
+          // a task's first tile always sets the maxima (every row starts at
+          // -inf and the task has live keys): one barrier, for lost waits only
+          if (named_sync_or(1, kSoftmaxThreads, !ok))
+            alive = false;
+          else
+            rescale = true;
+        } else if (named_sync_or(1, kSoftmaxThreads, need || !ok)) {
           if (named_sync_or(1, kSoftmaxThreads, !ok))
             alive = false;
           else
