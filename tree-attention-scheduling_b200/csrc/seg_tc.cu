@@ -28,7 +28,9 @@
 //               O_t is rescaled in TMEM only when a row's running max grows by
 //               more than 2^8 (otherwise the stale max is kept, which is exact
 //               after the final division).  Epilogue: O_t / z and the
-//               natural-log LSE per row.
+//               natural-log LSE per row; a full tile is staged (swizzled) in
+//               a K or V ring the tile no longer needs and leaves by four TMA
+//               stores, a partial tile by 32-byte stores per thread.
 //
 // Ordering facts the barrier scheme relies on: tcgen05.mma operations issued
 // by one thread execute in issue order, so S_t(j+1) cannot overwrite P_t(j)
@@ -142,7 +144,8 @@ __device__ __forceinline__ uint32_t swz_offset(int r, int c) {
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     seg_tc_kernel(SegParams p, const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                  const __grid_constant__ CUtensorMap tmap_q, int q_map_ok) {
+                  const __grid_constant__ CUtensorMap tmap_q, int q_map_ok,
+                  const __grid_constant__ CUtensorMap tmap_part, int part_map_ok) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::off_bar);
@@ -482,6 +485,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + o_col + c * 32, oa[c]);
       tmem_wait_ld();
+      if (part_map_ok && (t + 1) * kRows <= rows) {
+        // A full tile leaves by four TMA stores (32 columns x 128 rows each,
+        // 128-byte swizzled) staged in a ring this tile no longer needs: all S
+        // and P.V MMAs have completed once P.V_t(last) has, so tile A reuses
+        // the K ring and tile B the V ring.
+        unsigned char* stage = smem + (t == 0 ? TcSmem::off_k : TcSmem::off_v);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          unsigned char* box_row = stage + c * (kRows * 128) + row * 128;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(box_row + ((i ^ (row & 7)) << 4)) =
+                make_float4(__uint_as_float(oa[c][4 * i]) * inv, __uint_as_float(oa[c][4 * i + 1]) * inv,
+                            __uint_as_float(oa[c][4 * i + 2]) * inv, __uint_as_float(oa[c][4 * i + 3]) * inv);
+        }
+        fence_async_smem();
+        named_sync(1 + t, kSoftmaxWarps / 2 * 32);
+        if (quad == 0 && lane == 0) {
+          const int y = int(head_rows + part_row0 + t * kRows);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tma_store_2d(&tmap_part, stage + c * (kRows * 128), 32 * c, y);
+          bulk_commit_group();
+          bulk_wait_read_all();               // shared memory must outlive the reads
+        }
+      } else {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint32_t (&o)[32] = oa[c];
@@ -502,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                               __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
           }
         }
+      }
       }
       if (trow < rows)
         p.lse[head_rows + part_row0 + trow] = (alive && z > 0.f) ? (m_run + fast_log2(z)) * kLn2 : -INFINITY;
@@ -525,6 +554,11 @@ cudaError_t launch_typed(const SegParams& p, int num_tasks, cudaStream_t stream)
   // query tiles by TMA when G divides the 128-row tile (else per-thread loads)
   const int q_map_ok = make_query_map(&tq, p.q, p.num_requests, p.num_q_heads, p.group) ? 1 : 0;
   if (!q_map_ok) tq = tk;
+  // full 128-row tiles of partial outputs by TMA store
+  CUtensorMap tpart;
+  const int part_map_ok =
+      make_partial_map(&tpart, p.part, int64_t(p.num_kv_heads) * p.num_partials * p.group) ? 1 : 0;
+  if (!part_map_ok) tpart = tk;
   auto kernel = seg_tc_kernel<T>;
   static bool configured = false;
   if (!configured) {
@@ -533,7 +567,8 @@ cudaError_t launch_typed(const SegParams& p, int num_tasks, cudaStream_t stream)
     configured = true;
   }
   dim3 grid(num_tasks, p.num_kv_heads);
-  cudaError_t err = launch_dependent(kernel, grid, dim3(kThreads), TcSmem::alloc, stream, p, tk, tv, tq, q_map_ok);
+  cudaError_t err = launch_dependent(kernel, grid, dim3(kThreads), TcSmem::alloc, stream, p, tk, tv, tq, q_map_ok,
+                                     tpart, part_map_ok);
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }

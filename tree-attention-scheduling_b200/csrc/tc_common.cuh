@@ -151,6 +151,19 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Tiled 2-D TMA store from this CTA's shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store has finished READING shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // L2 policy that marks lines for early eviction (data read once).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t policy;
@@ -243,6 +256,22 @@ inline bool make_pool_map(CUtensorMap* map, const void* base, int64_t tokens, in
   cuuint32_t box[3] = {64, cuuint32_t(box_rows), 1};
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Partial outputs [rows, 128] f32 as a 2-D map with boxes of 32 columns x 128
+// rows (the 128-byte swizzle limits a box row to 128 bytes): four boxes store
+// one 128-row tile.
+inline bool make_partial_map(CUtensorMap* map, float* part, int64_t rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || rows <= 0 || rows > (int64_t(1) << 31)) return false;
+  cuuint64_t dims[2] = {128, cuuint64_t(rows)};
+  cuuint64_t strides[1] = {128 * 4};
+  cuuint32_t box[2] = {32, 128};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, part, dims, strides, box, elem,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
