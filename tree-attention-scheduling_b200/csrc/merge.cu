@@ -17,19 +17,21 @@ constexpr int kMergeWarps = 4;
 template <typename T, int D>
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) {
   constexpr int DL = D / 32;
-  pdl_wait();                // the segment kernels before this one have completed
-  pdl_trigger();             // the next step's query-tile kernel may set up meanwhile (it waits before any data)
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
-  if (item >= p.num_requests * p.num_q_heads) return;
-  const int request = item / p.num_q_heads, head = item % p.num_q_heads;
+  const bool active = item < p.num_requests * p.num_q_heads;
+  const int request = active ? item / p.num_q_heads : 0, head = active ? item % p.num_q_heads : 0;
   const int G = p.group, kv_head = head / G, g = head % G;
 
-  // The slot list is loaded together with the count (slot loads past the
-  // count are discarded), so the chain is count+slots -> LSEs -> rows.
+  // The count and the slot list are plan metadata, which no kernel writes: they
+  // are loaded before waiting for the segment kernels (slot loads past the
+  // count are discarded), so after the wait the chain is LSEs -> rows.
   const int32_t* slots = p.cslots + int64_t(request) * p.max_slots;
-  int count = p.counts[request];
-  const int pre_slot = lane < p.max_slots ? slots[lane] : -1;
+  int count = active ? p.counts[request] : 0;
+  const int pre_slot = active && lane < p.max_slots ? slots[lane] : -1;
+  pdl_wait();                // the segment kernels before this one have completed
+  pdl_trigger();             // the next step's query-tile kernel may set up meanwhile (it waits before any data)
+  if (!active) return;
   if (count < 0 || count > p.max_slots) {
     if (lane == 0) set_status(p.status, TA_ERR_BOUNDS);
     count = 0;
