@@ -160,6 +160,15 @@ class Plan:
                 raise ValueError(f"Plan does not partition request {request}'s context")
 
 
+def _chain_tuple(chain):
+    """The children of a (last child, earlier chain) chain, first to last."""
+    out = []
+    while chain is not None:
+        out.append(chain[0])
+        chain = chain[1]
+    return tuple(reversed(out))
+
+
 class _Planner:
     """Memoised cost evaluation and the greedy / subset-DP recursions for one call."""
 
@@ -265,23 +274,30 @@ class _Planner:
         return total, tuple(pushed)
 
     def _solve_subsets(self, node, node_id, runs):
-        # states: detached-request count -> (best subtotal, pushed children)
-        states = {0: (0.0, ())}
+        # states: detached-request count -> (best subtotal, pushed children),
+        # the pushed children as a chain (last child, earlier chain) so that
+        # extending a state costs O(1); tuples are built once at the end, where
+        # ties between totals are broken by the pushed tuples as in the reference.
+        states = {0: (0.0, None)}
         for child in node.children:
             count = self.node_size[child]
             apart = self.solve("cube", child, ())[0]
             together = self.solve("cube", child, runs)[0]
             updated = {}
+            get = updated.get
             for removed, (subtotal, pushed) in states.items():
-                for extra, subcost, chosen in ((0, apart, pushed), (count, together, pushed + (child,))):
-                    slot = removed + extra
-                    value = subtotal + subcost
-                    best = updated.get(slot)
-                    if best is None or value < best[0]:
-                        updated[slot] = (value, chosen)
+                value = subtotal + apart
+                best = get(removed)
+                if best is None or value < best[0]:
+                    updated[removed] = (value, pushed)
+                slot = removed + count
+                value = subtotal + together
+                best = get(slot)
+                if best is None or value < best[0]:
+                    updated[slot] = (value, (child, pushed))
             states = updated
         size = self.node_size[node_id]
-        return min((subtotal + self.count_cost(size - removed, runs), pushed)
+        return min((subtotal + self.count_cost(size - removed, runs), _chain_tuple(pushed))
                    for removed, (subtotal, pushed) in states.items())
 
     # -- job materialisation -----------------------------------------------
