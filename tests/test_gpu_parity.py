@@ -139,6 +139,17 @@ def test_segment_partials_match_oracle():
             assert (l - l_ref[j]).abs().max() <= LSE_TOL
 
 
+def test_one_kv_head_many_partials():
+    """One KV head (the 8-GPU shard of the headline shape): the root is cut into many pieces, so each
+    request merges more partials than one warp's batch and the split merge kernel runs."""
+    tree = KVTree.synthetic([-1] + [0] * 64, [8128] + [32] * 64, list(range(1, 65)))
+    q, k, v = make_inputs(64, tree.storage_tokens, 4, 1, 128, torch.bfloat16, seed=11)
+    plan = schedule(tree, 4, 1, 128, "cube", CostModel.b200())
+    out, lse, p = run_kernel(q, k, v, plan, pool_pad=64)
+    assert p.layout.max_pslots > 24
+    check_against_oracle(q, k, v, tree.paths, out, lse)
+
+
 def test_large_group_rows():
     """256 requests sharing one prefix: a job of 1024 query rows (many row tiles)."""
     tree = KVTree.synthetic([-1] + [0] * 256, [700] + [3 + (i % 5) for i in range(256)], list(range(1, 257)))
