@@ -50,6 +50,19 @@ def test_argument_validation_without_gpu():
     assert lib.ta_update_tail_klen(None, None, -1, 0, 0, None, None) == _lib.ERR_ARG
     # an empty plan is a no-op
     assert lib.ta_segment(layout, 1024, None, None, None, 0, 32, 8, 128, 1, None, None, None, None) == 0
+    # keys-in-lanes CTA counts: the per-class counts must add up to kn_ctas
+    bad = _lib.PlanLayout.from_buffer_copy(layout)
+    bad.kn_ctas = 3
+    bad.kn_class_ctas[1] = 2
+    assert lib.ta_segment(bad, 1024, None, None, None, 0, 32, 8, 128, 1, None, None, None, None) == _lib.ERR_ARG
+    # the 16- to 64-row classes have no kernel in this build (checked after the pointers, which are
+    # fake but aligned here: nothing is launched)
+    reserved = _lib.PlanLayout.from_buffer_copy(layout)
+    reserved.num_kn_tasks, reserved.num_kn_segs, reserved.kn_ctas = 1, 1, 1
+    reserved.kn_class_ctas[2] = 1
+    fake = 1 << 20
+    assert lib.ta_segment(reserved, fake, fake, fake, fake, 0, 32, 8, 128, 1, fake, fake, None,
+                          None) == _lib.ERR_UNSUPPORTED
 
 
 def test_layout_struct_matches_header():
