@@ -69,7 +69,7 @@
 extern "C" {
 #endif
 
-#define TA_ABI_VERSION 4
+#define TA_ABI_VERSION 5
 
 #define TA_DTYPE_BF16 1
 #define TA_DTYPE_F16 2
@@ -80,7 +80,8 @@ extern "C" {
 #define TA_ERR_BOUNDS 4       /* device: plan index out of range, access skipped */
 #define TA_ERR_TIMEOUT 8      /* device: a bounded wait gave up */
 #define TA_ERR_UNSUPPORTED 16 /* host: shape or dtype without a kernel */
-#define TA_ERR_TOO_LARGE 32   /* host: the problem exceeds ta_attention_noalloc's fixed scratch */
+#define TA_ERR_TOO_LARGE 32   /* host: the problem exceeds ta_attention_noalloc's fixed scratch,
+                                 or ta_plan_build's meta_capacity */
 
 /* Size of the device scratch array behind ta_attention_noalloc, per GPU. */
 #define TA_NOALLOC_SCRATCH_BYTES (32u << 20)
@@ -192,6 +193,34 @@ int ta_attention_noalloc(const ta_plan_layout* plan, const int32_t* meta, const 
  */
 int ta_update_tail_klen(int32_t* klen, const int32_t* tail_jobs, int32_t num_tails, int32_t value,
                         int32_t num_jobs, int32_t* status, void* stream);
+
+/*
+ * Host-side plan builder: the metadata buffer and layout of a physical job list
+ * that ta_segment / ta_merge / ta_attention consume.  Replaces the array loops
+ * of the reference's prepare (kernels.py:103-141): qids, kids, qlen, klen,
+ * slots and counts are the reference's arrays bit for bit (kids holds each
+ * job's first position, kstart_stride 1); the execution pieces, compact partial
+ * slots and the query-tile, keys-in-lanes and SIMT task lists follow them.
+ *
+ * Job j (in the caller's order: the reference's small-first stable sort) is the
+ * requests job_reqs[job_req_offsets[j] .. job_req_offsets[j+1]) over the
+ * contiguous positions [job_k0[j], job_k0[j] + job_keys[j]).  groups = query
+ * heads per KV head; use_tc selects the tcgen05 routes (head_dim 128), else
+ * every job runs on the SIMT kernel; sms is the SM count the task lists are
+ * balanced for; jobs with job_k0 >= no_split_from stay one piece each (the
+ * growing decode tails; no_split_from < 0: none).
+ *
+ * meta receives the int32 buffer, every array on a 16-byte boundary at the
+ * layout's off_* offsets.  On TA_ERR_TOO_LARGE (meta_capacity below the
+ * need) nothing is written to meta; *meta_size and *layout are set either way.
+ * TA_ERR_ARG: an empty job, a request outside [0, num_requests), a
+ * non-positive count.  TA_ERR_UNSUPPORTED: a keys-in-lanes task above 64 rows.
+ * Pure host code: needs no GPU.
+ */
+int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_reqs, const int32_t* job_k0,
+                  const int32_t* job_keys, int32_t num_jobs, int32_t num_requests, int32_t groups,
+                  int32_t use_tc, int32_t num_kv_heads, int32_t sms, int64_t no_split_from, int32_t* meta,
+                  int64_t meta_capacity, int64_t* meta_size, ta_plan_layout* layout);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,159 @@
+"""The native plan builder (``ta_plan_build``, csrc/plan.cpp) against ``build_metadata``, bit for bit.
+
+``prepare`` uploads the native builder's buffer; ``build_metadata`` +
+``flatten_metadata`` is the Python statement of the same construction.  Both
+run on the host, so these tests need no GPU.
+"""
+import ctypes
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from tree_attention import CostModel, KVTree, schedule
+from tree_attention import _lib, kernels
+from tree_attention.schedule import Job, physical_jobs
+from tests.golden.make_golden import COST_MODELS, HEADS, METHODS, TREE_SPECS, build_tree
+
+
+class _Lib:
+    KVTree = KVTree
+
+
+def layout_dict(layout):
+    out = {}
+    for name, _ in layout._fields_:
+        value = getattr(layout, name)
+        out[name] = list(value) if not isinstance(value, int) else value
+    return out
+
+
+def assert_native_matches(jobs, nreq, groups, use_tc, heads, sms, no_split_from=None):
+    meta = kernels.build_metadata(jobs, nreq, groups, use_tc, heads, sms, no_split_from)
+    flat, layout = kernels.flatten_metadata(meta, nreq)
+    nflat, nlayout, nmeta = kernels._native_metadata(jobs, nreq, groups, use_tc, heads, sms, no_split_from)
+    assert layout_dict(nlayout) == layout_dict(layout)
+    assert nflat.dtype == np.int32
+    np.testing.assert_array_equal(nflat, flat)
+    for name in kernels._ORDER:
+        assert nmeta[name].shape == meta[name].shape, name
+        np.testing.assert_array_equal(nmeta[name], meta[name], err_msg=name)
+    for name in ("small_max_keys", "kn_ctas", "num_partials", "contiguous_k"):
+        assert nmeta[name] == meta[name], name
+    for name in ("small_class_end", "kn_class_ctas"):
+        np.testing.assert_array_equal(nmeta[name], meta[name], err_msg=name)
+
+
+def sorted_jobs(plan, groups):
+    jobs = physical_jobs(plan.jobs)
+    jobs.sort(key=lambda job: len(job.requests) * groups > 16)
+    return jobs
+
+
+CASES = [(spec["name"], m, h, method) for spec in TREE_SPECS for m in range(len(COST_MODELS))
+         for h in range(len(HEADS)) for method in METHODS
+         if not (spec["name"] == "headline" and method == "request")]
+
+
+@pytest.mark.parametrize("name,model,heads,method", CASES)
+def test_native_builder_matches_on_reference_trees(name, model, heads, method):
+    spec = next(s for s in TREE_SPECS if s["name"] == name)
+    qh, kh, d = HEADS[heads]
+    tree = build_tree(_Lib, spec)
+    plan = schedule(tree, qh, kh, d, method, CostModel(**COST_MODELS[model]))
+    groups = qh // kh
+    jobs = sorted_jobs(plan, groups)
+    nreq = len(tree.paths)
+    assert_native_matches(jobs, nreq, groups, d == 128, kh, 148)
+    # fewer SMs change the piece split and the CTA balance; the SIMT routes
+    assert_native_matches(jobs, nreq, groups, d == 128, kh, 5)
+    assert_native_matches(jobs, nreq, groups, False, kh, 148)
+
+
+def test_native_builder_matches_on_headline_plans():
+    tree = build_tree(_Lib, next(s for s in TREE_SPECS if s["name"] == "headline"))
+    for method in ("request", "cube"):
+        plan = schedule(tree, 32, 8, 128, method, CostModel.b200())
+        jobs = sorted_jobs(plan, 4)
+        for sms in (148, 132, 16):
+            assert_native_matches(jobs, 128, 4, True, 8, sms)
+        assert_native_matches(jobs, 128, 4, True, 4, 148)   # a two-GPU KV-head shard
+
+
+def test_native_builder_matches_with_decode_tails():
+    tree = build_tree(_Lib, next(s for s in TREE_SPECS if s["name"] == "decode_tree"))
+    plan = schedule(tree, 32, 8, 128, "cube", CostModel.b200())
+    prefix, nreq = tree.storage_tokens, len(tree.paths)
+    for steps in (1, 16, 4096):
+        tails = [Job((r,), tuple(range(prefix + r * steps, prefix + (r + 1) * steps))) for r in range(nreq)]
+        jobs = physical_jobs(plan.jobs + tails)
+        jobs.sort(key=lambda job: len(job.requests) * 4 > 16)
+        for no_split in (None, prefix, 0):
+            assert_native_matches(jobs, nreq, 4, True, 8, 148, no_split)
+
+
+def random_jobs(rng, nreq):
+    jobs = []
+    for _ in range(rng.randint(1, 40)):
+        size = rng.choice([1, 1, 2, 3, 4, 5, 8, rng.randint(1, nreq)])
+        size = min(size, nreq)
+        if rng.random() < 0.5:
+            start = rng.randint(0, nreq - size)
+            requests = tuple(range(start, start + size))
+        else:
+            requests = tuple(sorted(rng.sample(range(nreq), size)))
+        keys = rng.choice([1, 7, 31, 32, 33, 64, 65, 96, 127, 128, 129, 256, 1000, rng.randint(1, 9000)])
+        start = rng.randint(0, 50000)
+        jobs.append(Job(requests, tuple(range(start, start + keys))))
+    return jobs
+
+
+def test_native_builder_matches_on_random_job_lists():
+    rng = random.Random(20261202)
+    for case in range(400):
+        nreq = rng.randint(1, 96)
+        groups = rng.choice([1, 2, 4, 8, 16])
+        heads = rng.choice([1, 2, 4, 8])
+        jobs = random_jobs(rng, nreq)
+        jobs.sort(key=lambda job: len(job.requests) * groups > 16)
+        no_split = rng.choice([None, None, 0, rng.randint(0, 50000)])
+        sms = rng.choice([1, 2, 7, 148])
+        assert_native_matches(jobs, nreq, groups, rng.random() < 0.8, heads, sms, no_split)
+
+
+def test_prepare_uses_the_native_buffer():
+    tree = build_tree(_Lib, next(s for s in TREE_SPECS if s["name"] == "small_config1"))
+    plan = schedule(tree, 32, 8, 128, "cube", CostModel.b200())
+    p = kernels.prepare(plan, torch.empty(len(tree.paths), 32, 128, dtype=torch.bfloat16))
+    meta = kernels.build_metadata(p.jobs, len(tree.paths), 4, True, 8, kernels._sm_count(torch.device("cpu")))
+    flat, layout = kernels.flatten_metadata(meta, len(tree.paths))
+    np.testing.assert_array_equal(p.metadata.numpy(), flat)
+    assert layout_dict(p.layout) == layout_dict(layout)
+
+
+def test_plan_build_rejects_bad_arguments():
+    lib = _lib.load()
+    offs = np.array([0, 2], dtype=np.int32)
+    reqs = np.array([0, 1], dtype=np.int32)
+    k0 = np.array([0], dtype=np.int32)
+    keys = np.array([100], dtype=np.int32)
+    size = ctypes.c_int64(-1)
+    layout = _lib.PlanLayout()
+
+    def call(nreq=2, offs=offs, reqs=reqs, keys=keys, num_jobs=1, groups=4, capacity=0, meta=None):
+        return lib.ta_plan_build(offs.ctypes.data, reqs.ctypes.data, k0.ctypes.data, keys.ctypes.data, num_jobs,
+                                 nreq, groups, 1, 8, 148, -1, meta, capacity, ctypes.byref(size),
+                                 ctypes.byref(layout))
+
+    # too small a buffer: the size and layout are reported, nothing written
+    assert call() == _lib.ERR_TOO_LARGE and size.value > 0 and layout.num_jobs == 1
+    buf = np.full(size.value, -7, dtype=np.int32)
+    assert call(capacity=size.value, meta=buf.ctypes.data) == 0
+    assert buf[layout.off_qids:layout.off_qids + 2].tolist() == [0, 1]
+    assert call(nreq=1) == _lib.ERR_ARG                                  # request 1 outside a batch of 1
+    assert call(num_jobs=0) == _lib.ERR_ARG
+    assert call(groups=0) == _lib.ERR_ARG
+    assert call(keys=np.array([0], dtype=np.int32)) == _lib.ERR_ARG    # empty job
+    assert call(offs=np.array([0, 0], dtype=np.int32)) == _lib.ERR_ARG  # job without requests
+    assert lib.ta_plan_build(None, None, None, None, 1, 1, 1, 1, 1, 1, -1, None, 0, None, None) == _lib.ERR_ARG

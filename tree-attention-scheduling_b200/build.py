@@ -1,6 +1,6 @@
 """Build the sm_100a kernel library in-tree: ``tree_attention/libtree_attn_b200.so``.
 
-Plain ``nvcc -shared`` over ``csrc/*.cu`` (static CUDA runtime, so the library
+Plain ``nvcc -shared`` over ``csrc/*.cu`` and the host-only ``csrc/*.cpp`` (static CUDA runtime, so the library
 is self-contained behind its C ABI; streams are passed in as cudaStream_t).
 Run ``python build.py`` or call ``build()``; rebuilds only when a source or the
 public header is newer than the library.
@@ -33,7 +33,7 @@ def nvcc_path():
 
 
 def sources():
-    return sorted(CSRC.glob("*.cu"))
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
 
 
 def _stale():

@@ -56,6 +56,7 @@ const char* ta_error_string(int code) {
     case TA_ERR_BOUNDS: return "plan index out of range on the device";
     case TA_ERR_TIMEOUT: return "bounded device wait gave up";
     case TA_ERR_UNSUPPORTED: return "shape or dtype not supported";
+    case TA_ERR_TOO_LARGE: return "problem exceeds a fixed scratch or buffer size";
     default: return "multiple errors";
   }
 }

@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libtree_attn_b200.so")
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 DTYPE_BF16 = 1
 DTYPE_F16 = 2
@@ -28,11 +28,11 @@ STATUS_NAMES = {ERR_ARG: "invalid argument", ERR_LAUNCH: "kernel launch failed",
                 ERR_BOUNDS: "plan index out of range on the device",
                 ERR_TIMEOUT: "bounded device wait gave up",
                 ERR_UNSUPPORTED: "shape or dtype not supported",
-                ERR_TOO_LARGE: "problem exceeds the fixed no-allocation scratch"}
+                ERR_TOO_LARGE: "problem exceeds a fixed scratch or buffer size"}
 
 # Every symbol declared in include/tree_attn.h.
 EXPORTS = ("ta_abi_version", "ta_error_string", "ta_segment", "ta_merge", "ta_attention",
-           "ta_attention_noalloc", "ta_update_tail_klen")
+           "ta_attention_noalloc", "ta_update_tail_klen", "ta_plan_build")
 
 
 class PlanLayout(ctypes.Structure):
@@ -82,6 +82,9 @@ def load():
     lib.ta_attention_noalloc.argtypes = [LP, P, P, P, P, I64, I32, I32, I32, I32, P, P, P, P]
     lib.ta_update_tail_klen.restype = ctypes.c_int
     lib.ta_update_tail_klen.argtypes = [P, P, I32, I32, I32, P, P]
+    lib.ta_plan_build.restype = ctypes.c_int
+    lib.ta_plan_build.argtypes = [P, P, P, P, I32, I32, I32, I32, I32, I32, I64, P, I64,
+                                  ctypes.POINTER(ctypes.c_int64), LP]
     version = lib.ta_abi_version()
     if version != ABI_VERSION:
         raise RuntimeError(f"kernel library ABI {version}, expected {ABI_VERSION}; rebuild it")

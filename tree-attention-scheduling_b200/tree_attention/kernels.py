@@ -25,8 +25,10 @@ point that launches work raises.
 """
 from __future__ import annotations
 
+import ctypes
 import os
 from dataclasses import dataclass, field
+from itertools import chain
 from math import ceil
 
 import numpy as np
@@ -254,6 +256,10 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
     slot), per-request partial counts and slots over pieces, SIMT tasks (piece,
     16-row tile) in three row classes, query-tile tasks (piece, 256-row pair)
     and the keys-in-lanes tasks (headers in persistent-CTA order, segment records).
+
+    This is the readable statement of the construction; ``prepare`` runs the
+    library's native ``ta_plan_build`` (``csrc/plan.cpp``), which tests hold
+    bit-identical to it (``flatten_metadata`` of this result).
     """
     njobs = len(jobs)
     maxr = max(len(j.requests) for j in jobs)
@@ -366,52 +372,39 @@ def _sm_count(device):
     return 148
 
 
-def prepare(plan, q, num_kv_heads=None, _no_split_from=None):
-    """Materialise ``plan`` for queries shaped like ``q`` ``[NREQ, HQ, D]`` (reference kernels.py:103-141).
+_SHAPES = {
+    "qids": lambda L: (L.num_jobs, L.max_requests), "kids": lambda L: (L.num_jobs, L.kstart_stride),
+    "qlen": lambda L: (L.num_jobs,), "klen": lambda L: (L.num_jobs,),
+    "slots": lambda L: (L.num_requests, L.max_slots), "counts": lambda L: (L.num_requests,),
+    "pieces": lambda L: (L.num_pieces, 4), "pcounts": lambda L: (L.num_requests,),
+    "cslots": lambda L: (L.num_requests, L.max_pslots), "small_tasks": lambda L: (L.num_small_tasks, 2),
+    "tc_tasks": lambda L: (L.num_tc_tasks, 4), "kn_offsets": lambda L: (L.kn_ctas + 1,),
+    "kn_tasks": lambda L: (L.num_kn_tasks, 4), "kn_segs": lambda L: (L.num_kn_segs, 12)}
+_OFFSET_FIELD = {name: "off_" + ("kstart" if name == "kids" else name) for name in _ORDER}
 
-    ``num_kv_heads`` defaults to ``plan.settings["kvheads"]``; a KV-head shard
-    passes its local head count (the plan itself is head independent).
+
+def flatten_metadata(meta, num_requests):
+    """``build_metadata``'s arrays as ``prepare``'s single int32 buffer and its layout.
+
+    Every array starts on a 16-byte boundary, in ``_ORDER``.  The native builder
+    produces exactly this buffer; tests compare the two.
     """
-    jobs = physical_jobs(plan.jobs)
-    kvheads = num_kv_heads or plan.settings["kvheads"]
-    nreq, hq, dim = q.shape
-    if hq % kvheads:
-        raise ValueError("Query heads must be divisible by KV heads")
-    groups = hq // kvheads
-    # Stable sort: small jobs (<= 16 query rows) first, as the reference does.
-    jobs.sort(key=lambda job: len(job.requests) * groups > _REF_SMALL_ROWS)
-    small_jobs = sum(len(job.requests) * groups <= _REF_SMALL_ROWS for job in jobs)
-    for job in jobs:
-        if not job.requests or not job.tokens:
-            raise ValueError("Plan contains an empty job")
-        if any(r < 0 or r >= nreq for r in job.requests):
-            raise ValueError("Plan references a request outside the query batch")
-    meta = build_metadata(jobs, nreq, groups, tc_supported(dim, q.dtype), kvheads, _sm_count(q.device),
-                          _no_split_from)
-    if not meta["contiguous_k"]:
-        raise ValueError("Physical jobs must read contiguous KV positions")
-
-    offsets, pieces, offset = {}, [], 0
+    offsets, parts, offset = {}, [], 0
     for name in _ORDER:
         array = meta[name]
         pad = -offset % 4                 # every array starts on a 16-byte boundary
         if pad:
-            pieces.append(np.zeros(pad, dtype=np.int32))
+            parts.append(np.zeros(pad, dtype=np.int32))
             offset += pad
         offsets[name] = offset
-        pieces.append(array.ravel())
+        parts.append(array.ravel())
         offset += array.size
-    flat = np.concatenate(pieces) if offset else np.zeros(0, dtype=np.int32)
-    device = q.device
-    metadata = torch.from_numpy(flat).to(device)
-    views = {name: metadata[offsets[name]:offsets[name] + meta[name].size].view(meta[name].shape)
-             for name in _ORDER}
-
+    flat = np.concatenate(parts) if offset else np.zeros(0, dtype=np.int32)
     layout = _lib.PlanLayout()
-    layout.num_jobs = len(jobs)
+    layout.num_jobs = meta["qids"].shape[0]
     layout.max_requests = meta["qids"].shape[1]
     layout.max_slots = meta["slots"].shape[1]
-    layout.num_requests = nreq
+    layout.num_requests = num_requests
     layout.num_pieces = meta["pieces"].shape[0]
     layout.num_partials = meta["num_partials"]
     layout.max_pslots = meta["cslots"].shape[1]
@@ -426,20 +419,80 @@ def prepare(plan, q, num_kv_heads=None, _no_split_from=None):
         layout.small_class_end[i] = int(meta["small_class_end"][i])
     layout.small_max_keys = meta["small_max_keys"]
     layout.kstart_stride = meta["kids"].shape[1]
-    layout.off_qids = offsets["qids"]
-    layout.off_kstart = offsets["kids"]
-    layout.off_qlen = offsets["qlen"]
-    layout.off_klen = offsets["klen"]
-    layout.off_slots = offsets["slots"]
-    layout.off_counts = offsets["counts"]
-    layout.off_pieces = offsets["pieces"]
-    layout.off_pcounts = offsets["pcounts"]
-    layout.off_cslots = offsets["cslots"]
-    layout.off_small_tasks = offsets["small_tasks"]
-    layout.off_tc_tasks = offsets["tc_tasks"]
-    layout.off_kn_offsets = offsets["kn_offsets"]
-    layout.off_kn_tasks = offsets["kn_tasks"]
-    layout.off_kn_segs = offsets["kn_segs"]
+    for name in _ORDER:
+        setattr(layout, _OFFSET_FIELD[name], offsets[name])
+    return flat, layout
+
+
+def _native_metadata(jobs, num_requests, groups, use_tc, heads, sms, no_split_from):
+    """``build_metadata`` + ``flatten_metadata`` by the library's ``ta_plan_build``.
+
+    Returns (flat int32 buffer, layout, the arrays as numpy views of the buffer).
+    """
+    lib = _lib.load()
+    njobs = len(jobs)
+    nq = np.fromiter((len(j.requests) for j in jobs), dtype=np.int32, count=njobs)
+    req_offsets = np.zeros(njobs + 1, dtype=np.int32)
+    np.cumsum(nq, out=req_offsets[1:])
+    reqs = np.fromiter(chain.from_iterable(j.requests for j in jobs), dtype=np.int32, count=int(req_offsets[-1]))
+    k0 = np.fromiter((j.tokens[0] for j in jobs), dtype=np.int32, count=njobs)
+    keys = np.fromiter((len(j.tokens) for j in jobs), dtype=np.int32, count=njobs)
+    layout = _lib.PlanLayout()
+    size = ctypes.c_int64(0)
+    capacity = 8 * (njobs + len(reqs)) * max(1, heads) + 4 * num_requests * 8 + 1024
+    for _ in range(2):
+        flat = np.empty(capacity, dtype=np.int32)
+        rc = lib.ta_plan_build(req_offsets.ctypes.data, reqs.ctypes.data, k0.ctypes.data, keys.ctypes.data, njobs,
+                               num_requests, groups, int(use_tc), heads, sms,
+                               -1 if no_split_from is None else int(no_split_from), flat.ctypes.data, capacity,
+                               ctypes.byref(size), ctypes.byref(layout))
+        if rc != _lib.ERR_TOO_LARGE:
+            break
+        capacity = size.value
+    _lib.check(rc, "ta_plan_build")
+    flat = flat[:size.value]
+    meta = {name: flat[getattr(layout, _OFFSET_FIELD[name]):].ravel()[:int(np.prod(_SHAPES[name](layout)))]
+            .reshape(_SHAPES[name](layout)) for name in _ORDER}
+    meta.update(small_class_end=np.array(layout.small_class_end[:], dtype=np.int32),
+                small_max_keys=layout.small_max_keys, kn_ctas=layout.kn_ctas,
+                kn_class_ctas=np.array(layout.kn_class_ctas[:], dtype=np.int32), contiguous_k=True,
+                num_partials=layout.num_partials)
+    return flat, layout, meta
+
+
+def prepare(plan, q, num_kv_heads=None, _no_split_from=None):
+    """Materialise ``plan`` for queries shaped like ``q`` ``[NREQ, HQ, D]`` (reference kernels.py:103-141).
+
+    ``num_kv_heads`` defaults to ``plan.settings["kvheads"]``; a KV-head shard
+    passes its local head count (the plan itself is head independent).  The
+    arrays are built by the library's native ``ta_plan_build`` (the construction
+    ``build_metadata`` states) and uploaded with one host-to-device copy.
+    """
+    jobs = physical_jobs(plan.jobs)
+    kvheads = num_kv_heads or plan.settings["kvheads"]
+    nreq, hq, dim = q.shape
+    if hq % kvheads:
+        raise ValueError("Query heads must be divisible by KV heads")
+    groups = hq // kvheads
+    # Stable sort: small jobs (<= 16 query rows) first, as the reference does.
+    jobs.sort(key=lambda job: len(job.requests) * groups > _REF_SMALL_ROWS)
+    small_jobs = sum(len(job.requests) * groups <= _REF_SMALL_ROWS for job in jobs)
+    if not jobs:
+        raise ValueError("Plan contains no jobs")
+    if not all(job.requests and job.tokens for job in jobs):
+        raise ValueError("Plan contains an empty job")
+    if not all(job.tokens[-1] - job.tokens[0] + 1 == len(job.tokens) for job in jobs):
+        raise ValueError("Physical jobs must read contiguous KV positions")
+    lo = min(min(job.requests) for job in jobs)
+    hi = max(max(job.requests) for job in jobs)
+    if lo < 0 or hi >= nreq:
+        raise ValueError("Plan references a request outside the query batch")
+    flat, layout, meta = _native_metadata(jobs, nreq, groups, tc_supported(dim, q.dtype), kvheads,
+                                          _sm_count(q.device), _no_split_from)
+    device = q.device
+    metadata = torch.from_numpy(flat).to(device)
+    views = {name: metadata[getattr(layout, _OFFSET_FIELD[name]):][:meta[name].size].view(meta[name].shape)
+             for name in _ORDER}
 
     rows = meta["num_partials"] * groups
     contiguous_q = all(j.requests[-1] - j.requests[0] + 1 == len(j.requests) for j in jobs)
