@@ -222,6 +222,43 @@ int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_reqs, const
                   int32_t use_tc, int32_t num_kv_heads, int32_t sms, int64_t no_split_from, int32_t* meta,
                   int64_t meta_capacity, int64_t* meta_size, ta_plan_layout* layout);
 
+/* Roofline constants of the tree scheduler's cost model (reference
+   schedule.py:29-39): bytes and FLOP per microsecond, per-task and per-partial
+   overheads, the small-group row and key tiles, the longest KV segment of a
+   job, and the large-group query-row tile (also the per-job request cap). */
+typedef struct ta_cost_model {
+  double bandwidth;
+  double cube_flops;
+  double task_us;
+  double merge_us;
+  int32_t cube_rows;
+  int32_t key_tile;
+  int32_t kv_split;
+  int32_t max_query_rows;
+} ta_cost_model;
+
+#define TA_SCHEDULE_GREEDY 1
+#define TA_SCHEDULE_CUBE 2
+
+/*
+ * Host-side tree scheduler: the greedy or subset-DP ("cube") recursion of the
+ * reference (schedule.py:96-143) with its job cost (schedule.py:41-52), run to
+ * the decisions its materialisation needs.  Node n (0 = root; children after
+ * their parent) has children children[child_offsets[n] .. child_offsets[n+1]),
+ * node_requests[n] requests passing through it, and its positions as maximal
+ * runs (first, length) = runs[2r], runs[2r+1] for r in [run_offsets[n],
+ * run_offsets[n+1]).  On return pushed[n] = 1 where the plan pushes the
+ * parent's inherited positions down into node n (the node's requests read them
+ * in its own jobs), else 0; *root_cost (may be NULL) is the root's estimated
+ * cost.  Every cost is computed as the reference's Python computes it (float
+ * sums compensated as CPython's sum() does), so plans, ties included, match.
+ * TA_ERR_ARG: a malformed tree or model.  Pure host code: needs no GPU.
+ */
+int ta_schedule_tree(const int32_t* child_offsets, const int32_t* children, const int32_t* node_requests,
+                     const int32_t* run_offsets, const int64_t* runs, int32_t num_nodes, int32_t method,
+                     const ta_cost_model* model, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                     uint8_t* pushed, double* root_cost);
+
 #ifdef __cplusplus
 }
 #endif

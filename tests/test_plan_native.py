@@ -1,8 +1,11 @@
-"""The native plan builder (``ta_plan_build``, csrc/plan.cpp) against ``build_metadata``, bit for bit.
+"""The native host planners against their Python statements, bit for bit.
 
-``prepare`` uploads the native builder's buffer; ``build_metadata`` +
-``flatten_metadata`` is the Python statement of the same construction.  Both
-run on the host, so these tests need no GPU.
+* ``ta_plan_build`` (csrc/plan.cpp) against ``build_metadata`` +
+  ``flatten_metadata``: ``prepare`` uploads the native builder's buffer.
+* ``ta_schedule_tree`` (csrc/schedule.cpp) against ``_Planner.solve``:
+  ``schedule`` takes its greedy / subset-DP decisions from the library.
+
+Both run on the host, so these tests need no GPU.
 """
 import ctypes
 import random
@@ -157,3 +160,93 @@ def test_plan_build_rejects_bad_arguments():
     assert call(keys=np.array([0], dtype=np.int32)) == _lib.ERR_ARG    # empty job
     assert call(offs=np.array([0, 0], dtype=np.int32)) == _lib.ERR_ARG  # job without requests
     assert lib.ta_plan_build(None, None, None, None, 1, 1, 1, 1, 1, 1, -1, None, 0, None, None) == _lib.ERR_ARG
+
+
+# ---- the native scheduler (ta_schedule_tree, csrc/schedule.cpp) against _Planner.solve ----
+
+def random_tree(rng):
+    """A random radix tree: random branching, node lengths (some zero-length roots) and terminals."""
+    n = rng.randint(2, 40)
+    parents, lengths = [-1], [rng.choice([0, rng.randint(1, 3000)])]
+    for i in range(1, n):
+        parents.append(rng.randint(max(0, i - rng.choice([1, 3, i])), i - 1))
+        lengths.append(rng.choice([1, 8, 31, 64, 129, rng.randint(1, 1200)]))
+    has_child = set(parents[1:])
+    terminals = [i for i in range(n) if i not in has_child]
+    terminals += [i for i in range(1, n) if i in has_child and rng.random() < 0.2]
+    rng.shuffle(terminals)
+    return KVTree.synthetic(parents, lengths, terminals)
+
+
+def random_model(rng):
+    return CostModel(bandwidth=rng.choice([900_000.0, 6_000_000.0, 6.5e6 * rng.random() + 1e5]),
+                     cube_flops=rng.choice([1e8, 1.2e9, 1.5e9 * rng.random() + 1e7]),
+                     task_us=rng.choice([0.15, 0.02, rng.random()]), merge_us=rng.choice([0.03, 0.002, 0.0]),
+                     cube_rows=rng.choice([4, 16, 32]), key_tile=rng.choice([64, 128, 256]),
+                     kv_split=rng.choice([48, 100, 512, 2048, 1 << 20]),
+                     max_query_rows=rng.choice([16, 64, 256, 512]))
+
+
+def assert_same_plan(tree, qh, kh, d, method, model):
+    native = schedule(tree, qh, kh, d, method, model)
+    spec = schedule(tree, qh, kh, d, method, model, _native=False)
+    assert native.jobs == spec.jobs
+    assert native.estimated_us == spec.estimated_us
+
+
+@pytest.mark.parametrize("method", ["greedy", "cube"])
+def test_native_scheduler_matches_on_random_trees(method):
+    rng = random.Random(7 if method == "cube" else 8)
+    for _ in range(150):
+        tree = random_tree(rng)
+        qh, kh, d = rng.choice([(32, 8, 128), (8, 2, 32), (16, 16, 64), (64, 4, 128)])
+        assert_same_plan(tree, qh, kh, d, method, random_model(rng))
+
+
+def test_native_scheduler_matches_on_bench_trees():
+    for name in ("headline", "decode_tree", "deep_bench", "wide", "no_share_root0"):
+        tree = build_tree(_Lib, next(s for s in TREE_SPECS if s["name"] == name))
+        for model in (CostModel(), CostModel.b200()):
+            for method in ("greedy", "cube"):
+                assert_same_plan(tree, 32, 8, 128, method, model)
+    # a decode tree grown one token per leaf and step (non-contiguous leaf runs)
+    tree = build_tree(_Lib, next(s for s in TREE_SPECS if s["name"] == "decode_tree"))
+    prefix, nreq = tree.storage_tokens, len(tree.paths)
+    leaves = list(range(len(tree.nodes) - nreq, len(tree.nodes)))
+    for step in range(3):
+        tree.extend_leaves(leaves, [prefix + r * 3 + step for r in range(nreq)])
+        assert_same_plan(tree, 32, 8, 128, "cube", CostModel.b200())
+
+
+def test_custom_cost_model_runs_the_python_recursion():
+    class Flat(CostModel):
+        def cost(self, requests, tokens, qheads, kvheads, dim):
+            return 1.0 if requests and tokens else 0.0
+
+    tree = build_tree(_Lib, next(s for s in TREE_SPECS if s["name"] == "deep_bench"))
+    plan = schedule(tree, 32, 8, 128, "cube", Flat())
+    assert plan.jobs == schedule(tree, 32, 8, 128, "cube", Flat(), _native=False).jobs
+    plan.validate(tree)
+
+
+def test_schedule_tree_rejects_bad_trees():
+    lib = _lib.load()
+    model = _lib.CostModelC(900_000.0, 1e8, 0.15, 0.03, 16, 128, 512, 64)
+    offs = np.array([0, 1, 1], dtype=np.int32)
+    kids = np.array([1], dtype=np.int32)
+    sizes = np.array([2, 1], dtype=np.int32)
+    roffs = np.array([0, 1, 2], dtype=np.int32)
+    runs = np.array([0, 10, 10, 5], dtype=np.int64)
+    pushed = np.full(2, 9, dtype=np.uint8)
+    cost = ctypes.c_double(0.0)
+
+    def call(kids=kids, runs=runs, method=_lib.SCHEDULE_CUBE, qh=32):
+        return lib.ta_schedule_tree(offs.ctypes.data, kids.ctypes.data, sizes.ctypes.data, roffs.ctypes.data,
+                                    runs.ctypes.data, 2, method, ctypes.byref(model), qh, 8, 128,
+                                    pushed.ctypes.data, ctypes.byref(cost))
+
+    assert call() == 0 and pushed.tolist() in ([0, 0], [0, 1]) and cost.value > 0
+    assert call(kids=np.array([0], dtype=np.int32)) == _lib.ERR_ARG          # a node its own child
+    assert call(runs=np.array([0, 10, 10, 0], dtype=np.int64)) == _lib.ERR_ARG  # an empty run
+    assert call(method=3) == _lib.ERR_ARG
+    assert call(qh=12) == _lib.ERR_ARG                                      # 12 query heads over 8 KV heads

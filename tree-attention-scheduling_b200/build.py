@@ -56,7 +56,9 @@ def build(force=False, verbose=False, extra_flags=()):
     objects = []
     for src in sources():
         obj = objdir / (src.stem + ".o")
-        cmd = [nvcc, *common, "-c", str(src), "-o", str(obj)]
+        # host-only planner sources: no FMA contraction, costs must round like the Python statement
+        host = ["-Xcompiler", "-ffp-contract=off"] if src.suffix == ".cpp" else []
+        cmd = [nvcc, *common, *host, "-c", str(src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

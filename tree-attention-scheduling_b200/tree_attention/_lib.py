@@ -32,7 +32,10 @@ STATUS_NAMES = {ERR_ARG: "invalid argument", ERR_LAUNCH: "kernel launch failed",
 
 # Every symbol declared in include/tree_attn.h.
 EXPORTS = ("ta_abi_version", "ta_error_string", "ta_segment", "ta_merge", "ta_attention",
-           "ta_attention_noalloc", "ta_update_tail_klen", "ta_plan_build")
+           "ta_attention_noalloc", "ta_update_tail_klen", "ta_plan_build", "ta_schedule_tree")
+
+SCHEDULE_GREEDY = 1
+SCHEDULE_CUBE = 2
 
 
 class PlanLayout(ctypes.Structure):
@@ -45,6 +48,13 @@ class PlanLayout(ctypes.Structure):
         "small_max_keys", "kstart_stride", "off_qids", "off_kstart", "off_qlen", "off_klen", "off_slots",
         "off_counts", "off_pieces", "off_pcounts", "off_cslots", "off_small_tasks", "off_tc_tasks",
         "off_kn_offsets", "off_kn_tasks", "off_kn_segs")]
+
+
+class CostModelC(ctypes.Structure):
+    """Mirror of ``ta_cost_model``."""
+    _fields_ = [("bandwidth", ctypes.c_double), ("cube_flops", ctypes.c_double), ("task_us", ctypes.c_double),
+                ("merge_us", ctypes.c_double), ("cube_rows", ctypes.c_int32), ("key_tile", ctypes.c_int32),
+                ("kv_split", ctypes.c_int32), ("max_query_rows", ctypes.c_int32)]
 
 
 def describe_status(code):
@@ -85,6 +95,9 @@ def load():
     lib.ta_plan_build.restype = ctypes.c_int
     lib.ta_plan_build.argtypes = [P, P, P, P, I32, I32, I32, I32, I32, I32, I64, P, I64,
                                   ctypes.POINTER(ctypes.c_int64), LP]
+    lib.ta_schedule_tree.restype = ctypes.c_int
+    lib.ta_schedule_tree.argtypes = [P, P, P, P, P, I32, I32, ctypes.POINTER(CostModelC), I32, I32, I32, P,
+                                     ctypes.POINTER(ctypes.c_double)]
     version = lib.ta_abi_version()
     if version != ABI_VERSION:
         raise RuntimeError(f"kernel library ABI {version}, expected {ABI_VERSION}; rebuild it")

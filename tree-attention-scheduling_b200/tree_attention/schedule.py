@@ -28,9 +28,13 @@ so that a plain ``schedule(tree)`` reproduces the reference's plan.
 """
 from __future__ import annotations
 
+import ctypes
 from collections import Counter
 from dataclasses import asdict, dataclass
+import itertools
 from math import ceil
+
+import numpy as np
 
 from .tree import KVTree
 
@@ -44,6 +48,10 @@ class Job:
 
 def _runs(positions):
     """Maximal runs ``(start, length)`` of consecutive positions, in order."""
+    n = len(positions)
+    if n > 16 and positions[-1] - positions[0] + 1 == n and tuple(positions) == tuple(range(positions[0],
+                                                                                            positions[0] + n)):
+        return ((positions[0], n),)      # one run, compared at C speed
     runs = []
     start = None
     length = 0
@@ -73,7 +81,10 @@ def _concat(a, b):
 
 
 def _expand(runs):
-    return tuple(p for start, length in runs for p in range(start, start + length))
+    if len(runs) == 1:
+        start, length = runs[0]
+        return tuple(range(start, start + length))
+    return tuple(itertools.chain.from_iterable(range(start, start + length) for start, length in runs))
 
 
 def physical_jobs(jobs):
@@ -182,6 +193,7 @@ class _Planner:
         self.kv_split = model.kv_split
         self.piece_memo = {}
         self.count_memo = {}
+        self.pieces_memo = {}
         self.solve_memo = {}
 
     # -- costs -------------------------------------------------------------
@@ -230,7 +242,9 @@ class _Planner:
         key = (count, runs)
         value = self.count_memo.get(key)
         if value is None:
-            pieces = self.chunk_pieces(runs)
+            pieces = self.pieces_memo.get(runs)
+            if pieces is None:
+                pieces = self.pieces_memo[runs] = self.chunk_pieces(runs)
             costs = []
             for q in range(0, count, self.req_tile):
                 nreq = min(self.req_tile, count - q)
@@ -308,14 +322,51 @@ class _Planner:
                 for q in range(0, len(requests), self.req_tile)
                 for k in range(0, len(tokens), self.kv_split)]
 
-    def materialize(self, method):
+    def native_pushed(self, method):
+        """Per node, whether the plan pushes its parent's positions into it, by ``ta_schedule_tree``.
+
+        The library runs the same recursion as ``solve`` (costs, sums and ties
+        computed identically); None when the cost model is not this module's
+        ``CostModel.cost`` (a subclass with its own formula runs ``solve``).
+        """
+        if type(self.model).cost is not CostModel.cost:
+            return None
+        from . import _lib
+        lib = _lib.load()
+        n = len(self.nodes)
+        child_offsets = np.zeros(n + 1, dtype=np.int32)
+        np.cumsum([len(node.children) for node in self.nodes], out=child_offsets[1:])
+        children = np.fromiter(itertools.chain.from_iterable(node.children for node in self.nodes),
+                               dtype=np.int32, count=int(child_offsets[-1]))
+        sizes = np.array(self.node_size, dtype=np.int32)
+        run_offsets = np.zeros(n + 1, dtype=np.int32)
+        np.cumsum([len(r) for r in self.node_runs], out=run_offsets[1:])
+        runs = np.fromiter(itertools.chain.from_iterable(p for r in self.node_runs for p in r), dtype=np.int64,
+                           count=2 * int(run_offsets[-1]))
+        m = self.model
+        model = _lib.CostModelC(m.bandwidth, m.cube_flops, m.task_us, m.merge_us, m.cube_rows, m.key_tile,
+                                m.kv_split, m.max_query_rows)
+        pushed = np.zeros(n, dtype=np.uint8)
+        rc = lib.ta_schedule_tree(child_offsets.ctypes.data, children.ctypes.data, sizes.ctypes.data,
+                                  run_offsets.ctypes.data, runs.ctypes.data, n,
+                                  _lib.SCHEDULE_CUBE if method == "cube" else _lib.SCHEDULE_GREEDY,
+                                  ctypes.byref(model), self.qheads, self.kvheads, self.dim, pushed.ctypes.data,
+                                  None)
+        _lib.check(rc, "ta_schedule_tree")
+        return pushed.tolist()
+
+    def materialize(self, method, native=True):
+        flags = self.native_pushed(method) if native else None
         jobs = []
         stack = [(0, ())]
         while stack:
             node_id, inherited = stack.pop()
             node = self.nodes[node_id]
             runs = _concat(inherited, self.node_runs[node_id])
-            _, pushed = self.solve(method, node_id, inherited)
+            if flags is None:
+                _, pushed = self.solve(method, node_id, inherited)
+            else:
+                pushed = tuple(c for c in node.children if flags[c])
             detached = {r for child in pushed for r in self.nodes[child].requests}
             remaining = tuple(r for r in node.requests if r not in detached)
             jobs.extend(self.split(remaining, runs))
@@ -329,8 +380,13 @@ class _Planner:
                    for j in physical_jobs(jobs))
 
 
-def schedule(tree: KVTree, qheads=32, kvheads=8, dim=128, method="cube", model=None):
-    """Plan the jobs of ``tree`` with ``method`` in {request, fixed, greedy, cube}."""
+def schedule(tree: KVTree, qheads=32, kvheads=8, dim=128, method="cube", model=None, _native=True):
+    """Plan the jobs of ``tree`` with ``method`` in {request, fixed, greedy, cube}.
+
+    The greedy and subset-DP decisions come from the library's native
+    ``ta_schedule_tree``; ``_native=False`` runs the Python statement of the
+    same recursion (``_Planner.solve``), which tests hold identical to it.
+    """
     if qheads % kvheads:
         raise ValueError("Query heads must be divisible by KV heads")
     model = model or CostModel()
@@ -340,7 +396,7 @@ def schedule(tree: KVTree, qheads=32, kvheads=8, dim=128, method="cube", model=N
     elif method == "fixed":
         jobs = [j for n in tree.nodes for j in planner.split(n.requests, n.tokens, runs=False)]
     elif method in ("greedy", "cube"):
-        jobs = planner.materialize(method)
+        jobs = planner.materialize(method, _native)
     else:
         raise ValueError(f"Unknown scheduling method: {method}")
     settings = asdict(model)
