@@ -9,7 +9,7 @@ the candidate constants, measures the resulting decode step on the GPU
 --config calibrate``) and keeps a candidate whose geometric-mean step time over
 the trees is lower by more than ``min_gain``.  The calibration trees
 (``workloads.calibration_grid``) share no request count, shared fraction or
-branching factor with the evaluation grid the fitted model is judged on.
+branching factor with the evaluation grid the fitted model is evaluated on.
 
 ``B200_CONSTANTS`` holds the result of the last fit (``python bench.py
 --config calibrate`` on one B200): from the previous constants it moved
