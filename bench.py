@@ -604,18 +604,21 @@ def run_qwen(args):
         barrier(world)
         eager_ms = max_over_ranks(e0.elapsed_time(e1) / eager_steps, world)
         # the decode step recorded once as a CUDA graph and replayed (device-side greedy loop).  Each
-        # generate() call captures its own graph and runs one eager warm-up step first; the replay cost
-        # per step is the difference between a 1-step and a `steps`-step call.
+        # generate() call captures its own graph and runs one eager warm-up step first; the per-step
+        # figure is timed around the replays alone (events recorded inside generate), the whole call
+        # (capture included) is reported beside it.
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
         def timed_generate(n):
             barrier(world)
             e0.record()
-            decoder.generate(n)
+            decoder.generate(n, events=(r0, r1))
             e1.record()
             barrier(world)
-            return max_over_ranks(e0.elapsed_time(e1), world)
-        one_ms = timed_generate(1)
-        all_ms = timed_generate(steps)
-        ms = (all_ms - one_ms) / (steps - 1)
+            return (max_over_ranks(e0.elapsed_time(e1), world),
+                    max_over_ranks(r0.elapsed_time(r1) / n, world))
+        one_ms, _ = timed_generate(1)
+        all_ms, ms = timed_generate(steps)
         results[method] = {"ms_per_step": round(ms, 3), "tokens_per_s": round(16 * 1000.0 / ms, 1),
                            "ms_per_step_incl_capture": round(all_ms / steps, 3),
                            "capture_and_first_step_ms": round(one_ms, 1),

@@ -195,6 +195,27 @@ int ta_update_tail_klen(int32_t* klen, const int32_t* tail_jobs, int32_t num_tai
                         int32_t num_jobs, int32_t* status, void* stream);
 
 /*
+ * One decode step's KV append for one layer, fused into one launch: for every
+ * request r < num_requests and KV head h < num_kv_heads, the new rows
+ * k_new[r * new_stride_request + h * new_stride_head + (0 .. head_dim)] (and
+ * likewise v_new; strides in elements, rows contiguous) are written to
+ * kpool / vpool [num_kv_heads, pool_tokens, head_dim] at position targets[r]
+ * (device int64).  Replaces the two index_copy_ calls of the reference's
+ * decode step (qwen.py:89-90).  When klen is not NULL the same launch also sets
+ * klen[tail_jobs[i]] = *count + offset for i < num_tails, with count a device
+ * int64: CachedDecodePlan.update (kernels.py:184-186) without a host value, so
+ * a captured step advances on the device.  A target outside [0, pool_tokens),
+ * a tail index outside [0, num_jobs) or a length outside int32 is skipped and
+ * TA_ERR_BOUNDS is OR-ed into *status.  Pointers must be 4-byte aligned and
+ * head_dim and the strides even (rows move as bf16/f16 pairs).
+ */
+int ta_decode_append(void* kpool, void* vpool, const void* k_new, const void* v_new, int64_t new_stride_request,
+                     int64_t new_stride_head, const int64_t* targets, int32_t num_requests, int32_t num_kv_heads,
+                     int64_t pool_tokens, int32_t head_dim, int32_t dtype, int32_t* klen, const int32_t* tail_jobs,
+                     int32_t num_tails, const int64_t* count, int32_t offset, int32_t num_jobs, int32_t* status,
+                     void* stream);
+
+/*
  * Host-side plan builder: the metadata buffer and layout of a physical job list
  * that ta_segment / ta_merge / ta_attention consume.  Replaces the array loops
  * of the reference's prepare (kernels.py:103-141): qids, kids, qlen, klen,

@@ -73,3 +73,22 @@ def test_layout_struct_matches_header():
     fields = [(n, int(c) if c else 1) for n, c in names]
     assert [(f[0], getattr(f[1], "_length_", 1)) for f in _lib.PlanLayout._fields_] == fields
     assert ctypes.sizeof(_lib.PlanLayout) == 4 * sum(c for _, c in fields)
+
+
+def test_decode_append_validation_without_gpu():
+    """ta_decode_append rejects bad arguments before any CUDA call."""
+    lib = _lib.load()
+    bf16 = _lib.DTYPE_BF16
+
+    def call(dtype=bf16, nreq=2, heads=8, dim=128, stride_r=1024, stride_h=128, ptr=4096, klen=None, tails=None,
+             count=None, num_tails=0):
+        return lib.ta_decode_append(ptr, ptr, ptr, ptr, stride_r, stride_h, ptr, nreq, heads, 64, dim, dtype, klen,
+                                    tails, num_tails, count, 1, 4, None, None)
+
+    assert call(dtype=7) == _lib.ERR_UNSUPPORTED
+    assert call(dim=127) == _lib.ERR_ARG            # rows move as bf16 pairs
+    assert call(stride_h=129) == _lib.ERR_ARG
+    assert call(heads=0) == _lib.ERR_ARG
+    assert call(ptr=4098) == _lib.ERR_ARG           # 2-byte aligned pointers
+    assert call(klen=4096) == _lib.ERR_ARG          # a tail update without tail indices / count
+    assert call(nreq=0) == 0                        # nothing to do, nothing launched

@@ -358,3 +358,45 @@ def test_decode_tree_plan_reuse_first_and_last_step():
             torch.cuda.synchronize()
             check_status(p)
             check_against_oracle(q, k, v, paths, out, lse.cpu())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_decode_append_matches_index_copy(dtype):
+    """The fused decode-step append writes the same pool rows as the reference's two index_copy_
+    calls, takes strided [NREQ, HK, D] rows, sets the tail lengths from a device count, and flags an
+    out-of-range target without writing it."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    hk, tokens, dim, nreq = 8, 300, 128, 5
+    kp = torch.randn(hk, tokens, dim, generator=g, device="cuda").to(dtype)
+    vp = torch.randn_like(kp)
+    # rows as the adapter has them: k[:, :, 0, :] of a [NREQ, HK, 1, D] view of a [NREQ, 1, HK, D] tensor
+    k4 = torch.randn(nreq, 1, hk, dim, generator=g, device="cuda").to(dtype).transpose(1, 2)
+    v4 = torch.randn(nreq, 1, hk, dim, generator=g, device="cuda").to(dtype).transpose(1, 2)
+    k_new, v_new = k4[:, :, 0, :], v4[:, :, 0, :]
+    targets = torch.tensor([7, 299, 0, 150, 42], device="cuda")
+    ref_k, ref_v = kp.clone(), vp.clone()
+    ref_k.index_copy_(1, targets, k_new.transpose(0, 1))
+    ref_v.index_copy_(1, targets, v_new.transpose(0, 1))
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kernels.append_kv(kp, vp, k_new, v_new, targets, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(kp, ref_k) and torch.equal(vp, ref_v)
+
+    # tail lengths of a cached plan from a device count, in the same launch
+    tree = KVTree.synthetic([-1, 0, 0], [64, 16, 16], [1, 2])
+    q = torch.empty(2, 32, 128, device="cuda", dtype=dtype)
+    cached = CachedDecodePlan(schedule(tree, method="cube"), q, tree.storage_tokens, 8)
+    count = torch.tensor([4], device="cuda")
+    kernels.append_kv(kp, vp, k_new, v_new, targets, None, (cached, count, 1))
+    torch.cuda.synchronize()
+    tails = cached.tail_indices.long()
+    assert cached.prepared.klen[tails].tolist() == [5, 5]
+    assert int(cached.prepared.status.item()) == 0
+
+    # an out-of-range target is skipped and flagged; the other rows are written
+    bad = torch.tensor([7, tokens, 0, 150, 42], device="cuda")
+    kernels.append_kv(kp, vp, torch.zeros_like(k_new), torch.zeros_like(v_new), bad, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & kernels._lib.ERR_BOUNDS
+    assert kp[:, 7].abs().sum().item() == 0 and torch.equal(kp[:, 299], ref_k[:, 299])

@@ -81,6 +81,7 @@ def _qwen_worker(rank, world, port, results):
         decoder = qwen.SharedKVDecoder(model, [list(s) for s in tq.SEQUENCES], max_new_tokens=3, method="cube",
                                        shard=(rank, world, None))
         qwen.attention_matrix = tq.oracle_attention(decoder)
+        qwen.append_kv = tq.reference_append
         logits = [decoder.logits.clone()]
         for _ in range(2):
             tokens = decoder.logits.argmax(-1).tolist()

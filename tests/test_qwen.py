@@ -40,6 +40,12 @@ def current_paths(decoder):
     return [tuple(p) for p in decoder.tree.paths]
 
 
+def reference_append(kp, vp, k_new, v_new, targets, status=None, tails=None):
+    """Stand-in for the fused append on CPU: the reference's two index_copy_ calls (qwen.py:89-90)."""
+    kp.index_copy_(1, targets, k_new.transpose(0, 1))
+    vp.index_copy_(1, targets, v_new.transpose(0, 1))
+
+
 def oracle_attention(decoder):
     """Stand-in for attention_matrix: FP32 attention over each request's current path."""
     def attention(q, kp, vp, prepared, out_lse=None):
@@ -59,6 +65,7 @@ def test_decoder_matches_full_forward_cpu(cached, prefill, monkeypatch):
         monkeypatch.setattr(qwen.CachedDecodePlan, "update", lambda self, n: self.prepared)
     decoder = cls(model, SEQUENCES, max_new_tokens=4, method="cube")
     monkeypatch.setattr(qwen, "attention_matrix", oracle_attention(decoder))
+    monkeypatch.setattr(qwen, "append_kv", reference_append)
     torch.testing.assert_close(decoder.logits, reference_logits(model, SEQUENCES), atol=1e-4, rtol=1e-4)
     for _ in range(3):
         tokens = decoder.logits.argmax(-1).tolist()
@@ -72,6 +79,7 @@ def test_decoder_capacity_and_shape_errors(monkeypatch):
     model = tiny_model(32, 4, 2, torch.float32, "cpu")
     decoder = qwen.SharedKVDecoder(model, SEQUENCES, max_new_tokens=1)
     monkeypatch.setattr(qwen, "attention_matrix", oracle_attention(decoder))
+    monkeypatch.setattr(qwen, "append_kv", reference_append)
     decoder.step([1] * len(SEQUENCES))
     with pytest.raises(ValueError):
         decoder.step([1] * len(SEQUENCES))          # exceeds max_new_tokens

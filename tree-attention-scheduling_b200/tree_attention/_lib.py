@@ -32,7 +32,7 @@ STATUS_NAMES = {ERR_ARG: "invalid argument", ERR_LAUNCH: "kernel launch failed",
 
 # Every symbol declared in include/tree_attn.h.
 EXPORTS = ("ta_abi_version", "ta_error_string", "ta_segment", "ta_merge", "ta_attention",
-           "ta_attention_noalloc", "ta_update_tail_klen", "ta_plan_build", "ta_schedule_tree")
+           "ta_attention_noalloc", "ta_update_tail_klen", "ta_decode_append", "ta_plan_build", "ta_schedule_tree")
 
 SCHEDULE_GREEDY = 1
 SCHEDULE_CUBE = 2
@@ -92,6 +92,8 @@ def load():
     lib.ta_attention_noalloc.argtypes = [LP, P, P, P, P, I64, I32, I32, I32, I32, P, P, P, P]
     lib.ta_update_tail_klen.restype = ctypes.c_int
     lib.ta_update_tail_klen.argtypes = [P, P, I32, I32, I32, P, P]
+    lib.ta_decode_append.restype = ctypes.c_int
+    lib.ta_decode_append.argtypes = [P, P, P, P, I64, I64, P, I32, I32, I64, I32, I32, P, P, I32, P, I32, I32, P, P]
     lib.ta_plan_build.restype = ctypes.c_int
     lib.ta_plan_build.argtypes = [P, P, P, P, I32, I32, I32, I32, I32, I32, I64, P, I64,
                                   ctypes.POINTER(ctypes.c_int64), LP]

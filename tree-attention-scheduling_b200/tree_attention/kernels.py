@@ -559,6 +559,44 @@ def attention_matrix(q, kp, vp, prepared, out_lse=None):
     return p.out
 
 
+def append_kv(kp, vp, k_new, v_new, targets, status=None, tails=None):
+    """Write one decode step's new K/V rows into the resident pools, in one launch (``ta_decode_append``).
+
+    ``k_new``/``v_new`` are ``[NREQ, HK, D]`` (rows contiguous, any request/head
+    strides), ``targets`` the int64 pool positions ``[NREQ]`` on the device: the
+    reference's ``kp.index_copy_`` / ``vp.index_copy_`` (qwen.py:89-90).
+    ``tails = (cached_plan, count, offset)`` also sets every tail length of a
+    ``CachedDecodePlan`` to ``count + offset`` (``count`` a device int64 tensor
+    of one element) in the same launch.  Out-of-range targets are skipped and
+    recorded in ``status`` (default: the cached plan's).
+    """
+    hk, tokens, dim = kp.shape
+    nreq = k_new.shape[0]
+    if (vp.shape != kp.shape or k_new.shape != (nreq, hk, dim) or v_new.shape != k_new.shape
+            or k_new.stride() != v_new.stride() or k_new.stride(2) != 1
+            or not (kp.is_contiguous() and vp.is_contiguous())):
+        raise ValueError("append_kv wants contiguous [HK, T, D] pools and [NREQ, HK, D] rows")
+    if not (k_new.dtype == v_new.dtype == kp.dtype == vp.dtype) or kp.dtype not in _DTYPES:
+        raise ValueError("append_kv: pools and rows must share one dtype, bfloat16 or float16")
+    if targets.dtype != torch.int64 or targets.shape != (nreq,):
+        raise ValueError("append_kv: targets must be int64 [NREQ]")
+    lib = _lib.load()
+    klen = tail_ids = count = None
+    offset = num_tails = num_jobs = 0
+    if tails is not None:
+        cached, count_t, offset = tails
+        p = cached.prepared
+        klen, tail_ids, count = p.klen.data_ptr(), cached.tail_indices.data_ptr(), count_t.data_ptr()
+        num_tails, num_jobs = cached.tail_indices.numel(), p.layout.num_jobs
+        status = p.status if status is None else status
+    stream = torch.cuda.current_stream(kp.device).cuda_stream
+    rc = lib.ta_decode_append(kp.data_ptr(), vp.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0),
+                              k_new.stride(1), targets.data_ptr(), nreq, hk, tokens, dim, _DTYPES[kp.dtype], klen,
+                              tail_ids, num_tails, count, int(offset), num_jobs,
+                              None if status is None else status.data_ptr(), stream)
+    _lib.check(rc, "ta_decode_append")
+
+
 def check_status(prepared):
     """Synchronise and raise if a kernel recorded a device-side error for this plan."""
     code = int(prepared.status.item())

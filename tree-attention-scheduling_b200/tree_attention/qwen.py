@@ -31,7 +31,7 @@ from types import MethodType
 
 import torch
 
-from .kernels import CachedDecodePlan, attention_matrix, prepare
+from .kernels import CachedDecodePlan, append_kv, attention_matrix, prepare
 from .schedule import CostModel, schedule
 from .tree import KVTree
 
@@ -207,10 +207,12 @@ class SharedKVDecoder:
         self.used += len(token_ids)
         return positions
 
-    def _attention_forward(self, prepared, targets, nreq):
+    def _attention_forward(self, prepared, targets, nreq, tails=None):
         """The decode-step attention of every layer: q/k/v projections (this rank's heads), q/k RMSNorm,
-        RoPE, append of the new K/V at ``targets`` (a device tensor of pool positions), tree attention
-        through ``attention_matrix`` and, when sharded, an all-gather of the heads before ``o_proj``."""
+        RoPE, append of the new K/V at ``targets`` (a device tensor of pool positions) by one fused launch,
+        tree attention through ``attention_matrix`` and, when sharded, an all-gather of the heads before
+        ``o_proj``.  ``tails = (cached_plan, count, offset)`` lets the first layer's append also set the
+        plan's tail lengths to ``count + offset`` on the device."""
         pools, slices, decoder = self.pools, self._slices, self
 
         def forward(module, hidden_states, position_embeddings, attention_mask=None, **kwargs):
@@ -232,8 +234,8 @@ class SharedKVDecoder:
             v = v.view(shape).transpose(1, 2)
             q, k = _rope(q, k, *position_embeddings)
             kp, vp = pools[module.layer_idx]
-            kp.index_copy_(1, targets, k[:, :, 0, :].transpose(0, 1))
-            vp.index_copy_(1, targets, v[:, :, 0, :].transpose(0, 1))
+            append_kv(kp, vp, k[:, :, 0, :], v[:, :, 0, :], targets, prepared.status,
+                      tails if module.layer_idx == 0 else None)
             result = attention_matrix(q[:, :, 0, :].contiguous(), kp, vp, prepared)
             if decoder.world > 1:
                 # rank-major concatenation along dim 0 (the form every backend accepts)
@@ -290,7 +292,7 @@ class CachedPrefixDecoder(SharedKVDecoder):
         return self.cached_plan.update(self.generated)
 
     @torch.inference_mode()
-    def generate(self, steps):
+    def generate(self, steps, events=None):
         """Greedy decode of ``steps`` tokens per request, the whole step recorded once as a CUDA graph.
 
         One replay feeds every request the argmax of its previous logits
@@ -299,7 +301,9 @@ class CachedPrefixDecoder(SharedKVDecoder):
         host round trip between steps.  Afterwards ``sequences``, ``logits``,
         ``generated`` and ``used`` are as ``steps`` calls of
         ``step(logits.argmax(-1))`` leave them.  Returns the generated tokens
-        ``[steps][NREQ]``.
+        ``[steps][NREQ]``.  ``events``, an optional (start, end) pair of
+        ``torch.cuda.Event(enable_timing=True)``, is recorded around the
+        replays alone (capture and warm-up excluded), for timing.
         """
         if steps <= 0:
             return []
@@ -315,14 +319,12 @@ class CachedPrefixDecoder(SharedKVDecoder):
         out = torch.zeros((steps, nreq), dtype=torch.int64, device=dev)
         positions = torch.empty((nreq, 1), dtype=torch.int64, device=dev)
         targets = torch.empty(nreq, dtype=torch.int64, device=dev)
-        tail_idx = self.cached_plan.tail_indices.long()
-        klen = self.cached_plan.prepared.klen
-        forward = self._attention_forward(self.cached_plan.prepared, targets, nreq)
+        # the first layer's fused append sets the tails' lengths to t + 1
+        forward = self._attention_forward(self.cached_plan.prepared, targets, nreq, (self.cached_plan, t, 1))
 
         def body():
             positions.copy_((start_pos + (t - t0))[:, None])
             targets.copy_(tail + t)
-            klen.index_copy_(0, tail_idx, (t + 1).to(torch.int32).expand(tail_idx.numel()))
             out.index_copy_(0, (t - t0).clamp(max=steps - 1), tokens[None])
             # a prepared (empty) mask mapping: the patched attention needs no mask, and building one
             # would copy a host scalar, which a graph capture cannot record
@@ -345,8 +347,12 @@ class CachedPrefixDecoder(SharedKVDecoder):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 logits = body()
+            if events is not None:
+                events[0].record()
             for _ in range(steps):
                 graph.replay()
+            if events is not None:
+                events[1].record()
             generated = out.tolist()
             self.logits = logits.clone()
             del graph
