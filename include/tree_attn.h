@@ -273,7 +273,8 @@ typedef struct ta_cost_model {
  * in its own jobs), else 0; *root_cost (may be NULL) is the root's estimated
  * cost.  Every cost is computed as the reference's Python computes it (float
  * sums compensated as CPython's sum() does), so plans, ties included, match.
- * TA_ERR_ARG: a malformed tree or model.  Pure host code: needs no GPU.
+ * TA_ERR_ARG: a malformed tree or model; TA_ERR_UNSUPPORTED: a tree deeper
+ * than 2000 levels.  Pure host code: needs no GPU.
  */
 int ta_schedule_tree(const int32_t* child_offsets, const int32_t* children, const int32_t* node_requests,
                      const int32_t* run_offsets, const int64_t* runs, int32_t num_nodes, int32_t method,

@@ -250,3 +250,23 @@ def test_schedule_tree_rejects_bad_trees():
     assert call(runs=np.array([0, 10, 10, 0], dtype=np.int64)) == _lib.ERR_ARG  # an empty run
     assert call(method=3) == _lib.ERR_ARG
     assert call(qh=12) == _lib.ERR_ARG                                      # 12 query heads over 8 KV heads
+
+
+def test_schedule_tree_bounds_its_depth():
+    """The native recursion follows the tree's depth on the caller's stack: a chain of 2000 levels
+    plans, a deeper one is rejected with an error code (no stack overflow)."""
+    lib = _lib.load()
+    model = _lib.CostModelC(900_000.0, 1e8, 0.15, 0.03, 16, 128, 512, 64)
+    for nodes, expected in ((2001, 0), (2002, _lib.ERR_UNSUPPORTED)):
+        offs = np.zeros(nodes + 1, dtype=np.int32)
+        offs[1:] = np.minimum(np.arange(1, nodes + 1), nodes - 1)     # node n's child is n + 1
+        kids = np.arange(1, nodes, dtype=np.int32)
+        sizes = np.ones(nodes, dtype=np.int32)
+        roffs = np.arange(nodes + 1, dtype=np.int32)
+        runs = np.stack([np.arange(nodes), np.ones(nodes, dtype=np.int64)], axis=1).astype(np.int64).ravel()
+        pushed = np.zeros(nodes, dtype=np.uint8)
+        for method in (_lib.SCHEDULE_GREEDY, _lib.SCHEDULE_CUBE):
+            rc = lib.ta_schedule_tree(offs.ctypes.data, kids.ctypes.data, sizes.ctypes.data, roffs.ctypes.data,
+                                      runs.ctypes.data, nodes, method, ctypes.byref(model), 32, 8, 128,
+                                      pushed.ctypes.data, None)
+            assert rc == expected, (nodes, method)

@@ -297,8 +297,13 @@ extern "C" int ta_schedule_tree(const int32_t* child_offsets, const int32_t* chi
   if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || head_dim <= 0) return TA_ERR_ARG;
   if (model->cube_rows <= 0 || model->key_tile < 2 || model->kv_split <= 0 || model->max_query_rows <= 0)
     return TA_ERR_ARG;
-  // every node but the root is the child of exactly one earlier node
+  // every node but the root is the child of exactly one earlier node.  The
+  // recursion follows the tree's depth on the caller's stack, so the depth is
+  // bounded (the Python statement stops at its recursion limit, about 500
+  // levels, far earlier)
+  constexpr int kMaxDepth = 2000;
   std::vector<char> seen(num_nodes, 0);
+  std::vector<int> depth(num_nodes, 0);
   for (int n = 0; n < num_nodes; ++n) {
     if (child_offsets[n + 1] < child_offsets[n] || run_offsets[n + 1] < run_offsets[n] || node_requests[n] < 0)
       return TA_ERR_ARG;
@@ -306,6 +311,8 @@ extern "C" int ta_schedule_tree(const int32_t* child_offsets, const int32_t* chi
       const int c = children[i];
       if (c <= n || c >= num_nodes || seen[c]) return TA_ERR_ARG;
       seen[c] = 1;
+      depth[c] = depth[n] + 1;
+      if (depth[c] > kMaxDepth) return TA_ERR_UNSUPPORTED;
     }
   }
   std::vector<Runs> node_runs(num_nodes);
