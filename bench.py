@@ -42,9 +42,17 @@ sys.path.insert(0, str(ROOT))
 
 import torch  # noqa: E402
 
-from tree_attention import CostModel, KVTree, schedule  # noqa: E402
-from tree_attention import kernels  # noqa: E402
-from tree_attention import _lib  # noqa: E402
+# The package (and with it the kernel library) is imported by the GPU arms
+# only: the reference arm runs nothing of this repository's engine.
+CostModel = KVTree = schedule = kernels = _lib = None
+
+
+def load_package():
+    """Import tree_attention for the GPU arms (binds the module-level names)."""
+    global CostModel, KVTree, schedule, kernels, _lib
+    from tree_attention import CostModel, KVTree, schedule  # noqa: F811
+    from tree_attention import kernels  # noqa: F811
+    from tree_attention import _lib  # noqa: F811
 
 METRIC = "tree-attn decode step µs & physical-KV HBM GB/s, 128req×8K ctx, 1–8 B200"
 NREQ, ROOT_LEN, LEAF_LEN = 128, 8128, 64
@@ -84,6 +92,13 @@ def profile_traffic():
         if line.startswith("traffic_bytes_per_step:"):
             return int(line.split(":", 1)[1].strip())
     return None
+
+
+def rank_traffic(local_heads):
+    """DRAM bytes of one rank's segment phase: the one-GPU capture scaled by the rank's share of KV heads
+    (every KV byte and partial row belongs to one head, so the traffic divides with the heads)."""
+    full = profile_traffic()
+    return None if full is None else int(round(full * local_heads / HK))
 
 
 # ---------------------------------------------------------------------------
@@ -418,7 +433,7 @@ def run_b200(args):
                 "eager_step_us": round(e2e_eager_us, 3)},
         "gpu_launches": step.launches * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(achieved / hbm_peak, 4), "traffic": profile_traffic(),
+                     "frac": round(achieved / hbm_peak, 4), "traffic": rank_traffic(len(heads)),
                      "kernel": "segment phase (all segment launches of one step)",
                      "peak_source": f"{peak_kind} hbm_gbs",
                      "tensor_tflops": round(logical_flops(tree, HQ * len(heads) // HK) / (seg_us * 1e-6) / 1e12, 1),
@@ -443,35 +458,59 @@ def run_b200(args):
         print(json.dumps(line), flush=True)
 
 
+class _Job:
+    """A job of the reference's plan: requests and physical token positions."""
+
+    def __init__(self, requests, runs):
+        self.requests = tuple(requests)
+        self.tokens = tuple(t for start, length in runs for t in range(start, start + length))
+
+
+def reference_headline_jobs():
+    """The reference's own cube plan of the headline tree (its default cost model), as recorded from the
+    reference itself in tests/golden/headline_plan.json."""
+    data = json.loads((ROOT / "tests" / "golden" / "headline_plan.json").read_text())
+    return [_Job(r, runs) for r, runs in data["jobs"]], data
+
+
 def run_reference(args):
-    """The reference's CPU implementation of the path (FP32 oracle port), rank 0 only."""
+    """The reference's CPU implementation of the path (FP32 oracle port), rank 0 only.
+
+    It plans with the reference's own scheduler and cost model (the plan the reference itself produced
+    for this tree, read from a committed fixture) and runs the plan-driven FP32 oracle on all host
+    threads; nothing of this repository's package or kernel library is imported.
+    """
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import attention as oracle
-    tree = headline_tree()
-    plan = schedule(tree, HQ, HK, D, args.method, CostModel.b200())
+    jobs, recorded = reference_headline_jobs()
+    storage = ROOT_LEN + NREQ * LEAF_LEN
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(SEED)
     q = torch.randn(NREQ, HQ, D, generator=g).bfloat16().float()
-    k = torch.randn(tree.storage_tokens, HK, D, generator=g).bfloat16().float()
-    v = torch.randn(tree.storage_tokens, HK, D, generator=g).bfloat16().float()
+    k = torch.randn(storage, HK, D, generator=g).bfloat16().float()
+    v = torch.randn(storage, HK, D, generator=g).bfloat16().float()
     for _ in range(args.warmup):
-        oracle.segmented_attention(q, k, v, plan.jobs)
+        oracle.segmented_attention(q, k, v, jobs)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.segmented_attention(q, k, v, plan.jobs)
+        oracle.segmented_attention(q, k, v, jobs)
     us = (time.perf_counter() - t0) * 1e6 / args.steps
-    value = kv_bytes(tree) / (us * 1e-6) / 1e9
+    value = storage * HK * D * 4 / (us * 1e-6) / 1e9
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": 0,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3), "step_us": round(us, 1),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1) BF16-valued Q/K/V)",
             "config": {"workload": "headline: 128 req x 8192 ctx, shared 8128-token root + 128 x 64-token leaves, "
-                                   "HQ=32 HK=8 D=128", "plan": args.method, "cost_model": "CostModel.b200()"},
+                                   "HQ=32 HK=8 D=128", "plan": "cube",
+                       "cost_model": "CostModel() (the reference's defaults)", "jobs": len(jobs),
+                       "plan_source": "the reference's own schedule() output, tests/golden/headline_plan.json "
+                                      f"(sha256 {recorded['digest'][:16]})"},
             "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": f"{args.steps} full headline steps of the FP32 plan-driven oracle"},
+                             "sample": f"{args.steps} full headline steps of the FP32 plan-driven oracle "
+                                       "(oracle/attention.py segmented_attention) on the reference's plan"},
             "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -737,7 +776,9 @@ def main():
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
         run_reference(args)
-    elif args.config == "grid":
+        return
+    load_package()
+    if args.config == "grid":
         run_grid(args)
     elif args.config == "decode":
         run_decode(args)

@@ -13,6 +13,9 @@ kernels.prepare on CPU tensors, reference) and records:
                     method x cost model x head configuration on those trees,
                     the 81-tree scan of ``scripts/scan_trees.py`` and the
                     reference's 81-tree evaluation grid (``scripts/tree_shapes.py``);
+* ``headline_plan.json`` the reference's cube plan of the headline tree with
+                    its default cost model, job by job (the reference arm of
+                    ``bench.py`` times the oracle on it);
 * ``prepare.npz``   the int32 metadata arrays of ``kernels.prepare``;
 * ``attention.npz`` seeded inputs with the FP32 outputs of
                     ``reference.request_attention`` / ``segmented_attention``.
@@ -125,12 +128,29 @@ def reference_grid_trees(ref):
         yield [parents, lengths, terminals]
 
 
-def main(reference_root):
+def headline_plan(ref, sched):
+    """The reference's own subset-DP plan of the headline tree with its default CostModel(), in full.
+
+    ``bench.py --impl reference`` times the FP32 oracle on this job list, so the reference arm plans
+    with the reference's scheduler and cost model and needs nothing from this repository's package.
+    """
+    spec = next(s for s in TREE_SPECS if s["name"] == "headline")
+    tree = build_tree(ref, spec)
+    plan = sched.schedule(tree, 32, 8, 128, "cube", sched.CostModel())
+    row = dump_plan(plan, full=True)
+    row.update(tree=spec["synthetic"], heads=[32, 8, 128], cost_model="CostModel() (reference defaults)")
+    return row
+
+
+def main(reference_root, only_headline=False):
     sys.path.insert(0, str(Path(reference_root) / "src"))
     ref = importlib.import_module("tree_attention")
     sched = importlib.import_module("tree_attention.schedule")
     kernels = importlib.import_module("tree_attention.kernels")
     oracle = importlib.import_module("tree_attention.reference")
+    (HERE / "headline_plan.json").write_text(json.dumps(headline_plan(ref, sched)))
+    if only_headline:
+        return
 
     trees, plans, prep = {}, [], {}
     for spec in TREE_SPECS:
@@ -210,6 +230,7 @@ def main(reference_root):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: python tests/golden/make_golden.py /path/to/tree-attention-scheduling")
-    main(sys.argv[1])
+    args = [a for a in sys.argv[1:] if a != "--headline-plan-only"]
+    if len(args) != 1:
+        sys.exit("usage: python tests/golden/make_golden.py [--headline-plan-only] /path/to/tree-attention-scheduling")
+    main(args[0], only_headline="--headline-plan-only" in sys.argv)

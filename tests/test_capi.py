@@ -92,3 +92,17 @@ def test_decode_append_validation_without_gpu():
     assert call(ptr=4098) == _lib.ERR_ARG           # 2-byte aligned pointers
     assert call(klen=4096) == _lib.ERR_ARG          # a tail update without tail indices / count
     assert call(nreq=0) == 0                        # nothing to do, nothing launched
+
+
+def test_noalloc_capacity_check_cannot_wrap_around():
+    """ta_attention_noalloc bounds its size arithmetic before multiplying (no CUDA call is reached)."""
+    lib = _lib.load()
+    layout = _lib.PlanLayout()
+    layout.kstart_stride = 1
+    layout.num_partials = 2 ** 31 - 1
+    # 2^31-1 partials x 2^30 query heads x 129 floats wraps a 64-bit size product: must still be rejected
+    assert lib.ta_attention_noalloc(layout, None, None, None, None, 0, 2 ** 30, 1, 128, _lib.DTYPE_BF16, None,
+                                    None, None, None) == _lib.ERR_TOO_LARGE
+    # head sizes without a kernel are rejected before the size check
+    assert lib.ta_attention_noalloc(layout, None, None, None, None, 0, 32, 8, 96, _lib.DTYPE_BF16, None,
+                                    None, None, None) == _lib.ERR_UNSUPPORTED

@@ -123,3 +123,22 @@ def test_physical_jobs_cuts_discontinuities():
     jobs = physical_jobs([Job((0,), (0, 1, 2, 5, 6, 9)), Job((1,), (3, 4))])
     assert [(j.requests, j.tokens) for j in jobs] == [((0,), (0, 1, 2)), ((0,), (5, 6)), ((0,), (9,)),
                                                       ((1,), (3, 4))]
+
+
+def test_reference_headline_plan_fixture():
+    """bench.py's reference arm times the oracle on the reference's own headline plan (headline_plan.json):
+    the fixture is that plan job by job, the same plan plans.json pins by digest, and the same plan this
+    package's scheduler produces with the reference's default cost model."""
+    recorded = json.loads((Path(__file__).parent / "golden" / "headline_plan.json").read_text())
+    assert plan_digest_of_runs(recorded["jobs"]) == recorded["digest"]
+    row = next(r for r in GOLDEN["plans"] if r["tree"] == "headline" and r["model"] == 0
+               and r["heads"] == [32, 8, 128] and r["method"] == "cube")
+    assert recorded["digest"] == row["plan"]["digest"] and recorded["njobs"] == row["plan"]["njobs"]
+    plan = schedule(tree_named("headline"), 32, 8, 128, "cube", CostModel())
+    assert [[list(j.requests), runs(j.tokens)] for j in plan.jobs] == recorded["jobs"]
+
+
+def plan_digest_of_runs(jobs):
+    import hashlib
+    canon = json.dumps(jobs, separators=(",", ":"))
+    return hashlib.sha256(canon.encode()).hexdigest()

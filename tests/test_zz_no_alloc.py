@@ -25,7 +25,7 @@ def _stream():
 
 
 def _inputs(seed=7):
-    # a shared root (tensor-core path) and private leaves (SIMT path)
+    # a shared root (query-tile kernel) and private leaves (small-group kernel)
     tree = KVTree.synthetic([-1] + [0] * 48, [900] + [20 + i for i in range(48)], list(range(1, 49)))
     g = torch.Generator().manual_seed(seed)
     q = torch.randn(48, 32, 128, generator=g).bfloat16().cuda()

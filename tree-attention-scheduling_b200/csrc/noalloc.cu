@@ -68,7 +68,12 @@ extern "C" int ta_attention_noalloc(const ta_plan_layout* plan, const int32_t* m
   if (!plan || plan->num_partials < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || head_dim <= 0 ||
       num_q_heads % num_kv_heads)
     return TA_ERR_ARG;
-  const size_t rows = size_t(plan->num_partials) * size_t(num_q_heads / num_kv_heads) * size_t(num_kv_heads);
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128) return TA_ERR_UNSUPPORTED;
+  // Partial rows = num_partials x G x num_kv_heads = num_partials x num_q_heads.
+  // Bound the factors before multiplying so no product can wrap around.
+  const size_t max_rows = kScratchBytes / ((size_t(head_dim) + 1) * sizeof(float));
+  if (size_t(plan->num_partials) > max_rows / size_t(num_q_heads)) return TA_ERR_TOO_LARGE;
+  const size_t rows = size_t(plan->num_partials) * size_t(num_q_heads);
   const size_t part_bytes = (rows * size_t(head_dim) * sizeof(float) + kAlign - 1) / kAlign * kAlign;
   const size_t lse_bytes = rows * sizeof(float);
   if (part_bytes + lse_bytes > kScratchBytes) return TA_ERR_TOO_LARGE;

@@ -157,34 +157,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int4 rec = reinterpret_cast<const int4*>(p.tc_tasks)[task];
   const int piece = rec.x, pair = rec.y;
-  Piece pc;
-  const int state = resolve_piece(p, piece, pc);
+  // Before the dependency wait only records that no kernel writes are read
+  // (task, piece, request count, slot): a job's key count may be rewritten by
+  // the kernel before this one (a decode step's append or tail update), so it
+  // is read after pdl_wait below.
+  PieceRows pr;
+  const bool addressable = resolve_piece_rows(p, piece, pr);
   const int r0 = pair * 2 * kRows;
-  const int rows = state == PIECE_SKIP ? 0 : min(2 * kRows, pc.nr * G - r0);   // rows of this pair
+  const int rows = addressable ? min(2 * kRows, pr.nr * G - r0) : 0;   // rows of this pair
   if (rows <= 0) {
     pdl_wait();
     if (tid == 0) set_status(p.status, TA_ERR_BOUNDS);
     return;
   }
-  if (state == PIECE_BAD_KEYS && tid == 0) set_status(p.status, TA_ERR_BOUNDS);
-  const int job = pc.job;
-  const int nk = pc.nk;
-  const int64_t k0 = pc.k0;
+  const int job = pr.job;
   const int ntile = rows > kRows ? 2 : 1;                  // tile B present?
-  const int64_t part_row0 = pc.slot * G + r0;
-  const int ntiles = (nk + kKeys - 1) / kKeys;
+  const int64_t part_row0 = pr.slot * G + r0;
   const int64_t head_rows = int64_t(head) * p.num_partials * G;
   // The job's requests are consecutive: the query tiles come in by TMA
   // (boxes of 128/G requests x G query heads), issued before the first K tile.
-  const int q0 = (rec.z >= 0 && int64_t(rec.z) + pc.nr <= p.num_requests) ? rec.z : -1;
+  const int q0 = (rec.z >= 0 && int64_t(rec.z) + pr.nr <= p.num_requests) ? rec.z : -1;
   const bool tma_q = q_map_ok && q0 >= 0;
-
-  if (ntiles == 0) {  // empty segment: O = 0, LSE = -inf
-    pdl_wait();
-    for (int i = tid; i < rows * kDim; i += kThreads) p.part[(head_rows + part_row0 + i / kDim) * kDim + i % kDim] = 0.f;
-    for (int i = tid; i < rows; i += kThreads) p.lse[head_rows + part_row0 + i] = -INFINITY;
-    return;
-  }
 
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -211,14 +204,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   bool alive = true;
   // This kernel may have been placed while the kernel before it (the previous
-  // step's merge) still runs; everything above read only this launch's plan
-  // records.  Queries, pools and partial outputs wait for its completion, and
-  // only then may the keys-in-lanes kernel be placed (it writes partials too).
-  // Every CTA, early exits included, waits before it triggers or exits.
+  // step's merge, or a decode step's KV append that rewrites the tails' key
+  // counts) still runs; everything above read only plan records no kernel
+  // writes.  Key counts, queries, pools and partial outputs wait for its
+  // completion, and only then may the next segment kernel be placed (it
+  // writes partials too).  Every CTA, early exits included, waits before it
+  // triggers or exits.
   pdl_wait();
   pdl_trigger();
+  Piece pc;
+  const int state = resolve_piece(p, piece, pc);
+  if (state == PIECE_BAD_KEYS && tid == 0) set_status(p.status, TA_ERR_BOUNDS);
+  const int nk = state == PIECE_OK ? pc.nk : 0;
+  const int64_t k0 = pc.k0;
+  const int ntiles = (nk + kKeys - 1) / kKeys;
 
-  if (warp == 0 || warp == kVProducerWarp) {
+  if (ntiles == 0) {  // empty segment: O = 0, LSE = -inf
+    for (int i = tid; i < rows * kDim; i += kThreads) p.part[(head_rows + part_row0 + i / kDim) * kDim + i % kDim] = 0.f;
+    for (int i = tid; i < rows; i += kThreads) p.lse[head_rows + part_row0 + i] = -INFINITY;
+  } else if (warp == 0 || warp == kVProducerWarp) {
     // ---------------- TMA producers (K ring / V ring) ----------------
     const bool is_k = warp == 0;
     if (lane == 0) {

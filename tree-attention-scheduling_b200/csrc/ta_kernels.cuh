@@ -43,6 +43,29 @@ struct Piece {
   int64_t slot;   // first partial slot
 };
 
+// The parts of a piece that no kernel writes: its job, request count and
+// first partial slot.
+struct PieceRows {
+  int job;
+  int nr;
+  int64_t slot;
+};
+
+// Resolve the fixed records of `piece` (no key count: that may be rewritten by
+// the kernel before).  False: its partial slots are not addressable, nothing
+// may be written.
+__device__ __forceinline__ bool resolve_piece_rows(const SegParams& p, int piece, PieceRows& out) {
+  if (piece < 0 || piece >= p.num_pieces) return false;
+  const int job = p.pieces[4 * piece], slot = p.pieces[4 * piece + 3];
+  if (job < 0 || job >= p.num_jobs) return false;
+  const int nr = p.qlen[job];
+  if (nr <= 0 || nr > p.max_requests || slot < 0 || int64_t(slot) + nr > p.num_partials) return false;
+  out.job = job;
+  out.nr = nr;
+  out.slot = slot;
+  return true;
+}
+
 // Outcome of resolve_piece.
 enum PieceState { PIECE_SKIP = 0, PIECE_OK = 1, PIECE_BAD_KEYS = 2 };
 

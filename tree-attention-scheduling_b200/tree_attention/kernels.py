@@ -580,12 +580,25 @@ def append_kv(kp, vp, k_new, v_new, targets, status=None, tails=None):
         raise ValueError("append_kv: pools and rows must share one dtype, bfloat16 or float16")
     if targets.dtype != torch.int64 or targets.shape != (nreq,):
         raise ValueError("append_kv: targets must be int64 [NREQ]")
+    # every pointer the kernel dereferences must be memory of the pools' GPU
+    device = kp.device
+    if device.type != "cuda" or any(t.device != device for t in (vp, k_new, v_new, targets)):
+        raise ValueError("append_kv: pools, rows and targets must be CUDA tensors on one device")
+    if status is not None and (status.device != device or status.dtype != torch.int32 or status.numel() < 1):
+        raise ValueError("append_kv: status must be an int32 CUDA tensor on the pools' device")
     lib = _lib.load()
     klen = tail_ids = count = None
     offset = num_tails = num_jobs = 0
     if tails is not None:
         cached, count_t, offset = tails
+        if count_t.device != device or count_t.dtype != torch.int64 or count_t.numel() < 1:
+            raise ValueError("append_kv: the step count must be an int64 tensor of at least one element "
+                             "on the pools' device")
+        if cached.tail_indices.device != device or cached.tail_indices.dtype != torch.int32:
+            raise ValueError("append_kv: the cached plan's tail indices must be int32 on the pools' device")
         p = cached.prepared
+        if p.klen.device != device:
+            raise ValueError("append_kv: the cached plan lives on another device than the pools")
         klen, tail_ids, count = p.klen.data_ptr(), cached.tail_indices.data_ptr(), count_t.data_ptr()
         num_tails, num_jobs = cached.tail_indices.numel(), p.layout.num_jobs
         status = p.status if status is None else status
