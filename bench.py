@@ -211,8 +211,22 @@ class Step:
         self.q, self.kp, self.vp = copies[0]
         self.lib = _lib.load()
         L = prepared.layout
-        self.launches = (sum(1 for i, e in enumerate(L.small_class_end) if e > (L.small_class_end[i - 1] if i else 0))
-                         + (1 if L.num_tc_tasks else 0) + sum(1 for c in range(5) if L.kn_class_ctas[c] > 0) + 1)
+        small = sum(1 for i, e in enumerate(L.small_class_end) if e > (L.small_class_end[i - 1] if i else 0))
+        if os.environ.get("TREE_ATTN_SMALL_KERNEL") != "stream":
+            kn, fused = sum(1 for c in range(5) if L.kn_class_ctas[c] > 0), False
+        else:   # one small-group launch, which also merges when it is the step's last launch
+            kn, fused = (1 if L.num_kn_segs else 0), L.num_kn_segs > 0 and small == 0
+        self.launches = small + (1 if L.num_tc_tasks else 0) + kn + (0 if fused else 1)
+
+    def attention(self, copy=0):
+        """The whole step through the public C entry point ta_attention."""
+        p = self.p
+        q, kp, vp = self.copies[copy]
+        rc = self.lib.ta_attention(p.layout, p.metadata.data_ptr(), q.data_ptr(), kp.data_ptr(), vp.data_ptr(),
+                                   kp.shape[1], q.shape[1], kp.shape[0], D, _lib.DTYPE_BF16, p.part.data_ptr(),
+                                   p.lse.data_ptr(), p.out.data_ptr(), None, p.status.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream)
+        _lib.check(rc, "ta_attention")
 
     def segment(self, copy=0):
         p = self.p
@@ -257,11 +271,12 @@ def time_graph(graph, units, warmup, world):
 
 
 def time_step(step, steps, warmup, world):
-    """Device time (us) per step: K whole steps in one graph, then the segment
-    launches and the merge alone (for the per-kernel roofline), all rotating
-    through the input copies so every step streams its KV from HBM."""
+    """Device time (us) per step: K whole steps (ta_attention) in one graph, then the
+    segment launches alone (ta_segment, for the per-kernel roofline) and the merge
+    kernel alone, all rotating through the input copies so every step streams its
+    KV from HBM."""
     n = len(step.copies)
-    whole = capture(lambda: [(step.segment(i % n), step.merge(i % n)) for i in range(steps)])
+    whole = capture(lambda: [step.attention(i % n) for i in range(steps)])
     step_us = time_graph(whole, steps, warmup, world)
     seg = capture(lambda: [step.segment(i % n) for i in range(steps)])
     seg_us = time_graph(seg, steps, warmup, world)
@@ -377,8 +392,7 @@ def run_b200(args):
     burn_end = time.perf_counter() + (0.0 if args.quick else args.burn_s)
     i = 0
     while time.perf_counter() < burn_end:       # sustained load so the clock samples see the step
-        step.segment(i % COPIES)
-        step.merge(i % COPIES)
+        step.attention(i % COPIES)
         i += 1
     step_us_local, seg_us, merge_us = time_step(step, args.steps, args.warmup, world)
     clocks = sampler.stop()
@@ -583,7 +597,7 @@ def run_calibrate(args):
         prepared = kernels.prepare(schedule(tree, HQ, HK, D, "cube", model), copies[0][0])
         step = Step(copies, prepared)
         n = len(copies)
-        graph = capture(lambda: [(step.segment(i % n), step.merge(i % n)) for i in range(steps)])
+        graph = capture(lambda: [step.attention(i % n) for i in range(steps)])
         us = time_graph(graph, steps, warmup, 1)
         kernels.check_status(prepared)
         del graph, step, prepared

@@ -227,8 +227,8 @@ def test_bounds_violation_is_reported_not_trapped():
 
 
 def test_headline_full_size_properties():
-    """Full BASELINE headline shape: tree plans agree with the per-request plan, and a
-    sample of requests agrees with the FP32 oracle."""
+    """Full BASELINE headline shape: tree plans agree with the per-request plan, and all 128
+    requests of every plan agree with the FP32 oracle."""
     tree = KVTree.synthetic([-1] + [0] * 128, [8128] + [64] * 128, list(range(1, 129)))
     q, k, v = make_inputs(128, tree.storage_tokens, 32, 8, 128, torch.bfloat16, seed=101)
     qd = q.cuda()
@@ -245,13 +245,13 @@ def test_headline_full_size_properties():
     for key, (o, l) in outs.items():
         assert rel_l2(o.cpu(), base_out.cpu()).max() <= REL_L2, key
         assert (l - base_lse).abs().max().item() <= LSE_TOL, key
-    sample = [0, 1, 63, 127]
-    sub_paths = [tree.paths[r] for r in sample]
-    _, ref_f, ref_lse = oracle.request_attention(q[sample].float(), k.float(), v.float(), sub_paths,
-                                                 return_lse=True)
+    # every request of every plan against the FP32 oracle (the oracle runs the 128 x 8192 shape in
+    # seconds on the host)
+    _, ref_f, ref_lse = oracle.request_attention(q.float(), k.float(), v.float(), tree.paths, return_lse=True)
     for key, (o, l) in outs.items():
-        assert rel_l2(o.cpu()[sample], ref_f).max() <= REL_L2, key
-        assert (l.cpu()[sample] - ref_lse).abs().max() <= LSE_TOL, key
+        assert rel_l2(o.cpu(), ref_f).max() <= REL_L2, key
+        assert (l.cpu() - ref_lse).abs().max() <= LSE_TOL, key
+        torch.testing.assert_close(o.cpu().float(), ref_f.to(o.dtype).float(), atol=.008, rtol=.03)
 
 
 @pytest.mark.parametrize("keys", [1, 100, 128, 129, 256, 384, 512, 640, 1000, 2048, 2600])
@@ -400,3 +400,94 @@ def test_decode_append_matches_index_copy(dtype):
     torch.cuda.synchronize()
     assert int(status.item()) & kernels._lib.ERR_BOUNDS
     assert kp[:, 7].abs().sum().item() == 0 and torch.equal(kp[:, 299], ref_k[:, 299])
+
+
+def _segment_then_merge(qd, kp, vp, p, lse_out):
+    """ta_segment and ta_merge as two calls (the merge kernel), for comparison with ta_attention."""
+    lib = kernels._lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    dt = kernels._DTYPES[qd.dtype]
+    hq, hk, d = qd.shape[1], kp.shape[0], qd.shape[2]
+    out = torch.empty_like(qd)
+    assert lib.ta_segment(p.layout, p.metadata.data_ptr(), qd.data_ptr(), kp.data_ptr(), vp.data_ptr(),
+                          kp.shape[1], hq, hk, d, dt, p.part.data_ptr(), p.lse.data_ptr(), p.status.data_ptr(),
+                          stream) == 0
+    assert lib.ta_merge(p.layout, p.metadata.data_ptr(), p.part.data_ptr(), p.lse.data_ptr(), out.data_ptr(),
+                        lse_out.data_ptr(), hq, hk, d, dt, p.status.data_ptr(), stream) == 0
+    return out
+
+
+def _queue(p):
+    return p.metadata[p.layout.off_queue:p.layout.off_queue + kernels.QUEUE_WORDS]
+
+
+@pytest.mark.parametrize("heads", [(8, 8), (16, 8), (32, 8), (64, 8)], ids=["G1", "G2", "G4", "G8"])
+def test_small_group_kernel_group_sizes(heads):
+    """The small-group kernel with 1, 2, 4 and 8 query heads per KV head: segments of up to 8 query
+    rows cut into four-row items (a request's rows split across items for G = 8, several requests per
+    item for G = 1 and 2), shared small groups and private leaves of 1..200 keys, fused merge and
+    separate merge kernel agreeing, queue counters back at zero after each call."""
+    hq, hk = heads
+    leaves = [1, 7, 16, 33, 64, 65, 127, 200]
+    parents = [-1, 0, 0] + [1] * 4 + [2] * 4
+    lengths = [40, 300, 9] + leaves
+    tree = KVTree.synthetic(parents, lengths, [3, 3, 4, 5, 6, 7, 8, 9, 10, 10])
+    q, k, v = make_inputs(len(tree.paths), tree.storage_tokens, hq, hk, 128, torch.bfloat16, seed=hq * 7)
+    qd = q.cuda()
+    kp, vp = pack_kv(k.cuda(), v.cuda())
+    for method in ("request", "cube", "fixed"):
+        plan = schedule(tree, hq, hk, 128, method, CostModel(kv_split=128))
+        p = prepare(plan, qd)
+        assert p.layout.num_kn_segs > 0
+        lse = torch.empty(len(tree.paths), hq, device="cuda")
+        out = attention_matrix(qd, kp, vp, p, out_lse=lse).clone()
+        torch.cuda.synchronize()
+        check_status(p)
+        assert int(_queue(p).abs().sum().item()) == 0
+        check_against_oracle(q, k, v, tree.paths, out.cpu(), lse.cpu())
+        lse2 = torch.empty_like(lse)
+        out2 = _segment_then_merge(qd, kp, vp, p, lse2)
+        torch.cuda.synchronize()
+        check_status(p)
+        assert int(_queue(p).abs().sum().item()) == 0
+        assert torch.equal(out2, out) and torch.equal(lse2, lse)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_small_group_kernel_beside_query_tiles(dtype):
+    """A shared root on the query-tile kernel and 300 private leaves on the small-group kernel, which
+    starts beside it; more segments than resident CTAs, so CTAs take several from the queue.  Ten
+    back-to-back calls and a graph replay of three give the same result as the first call."""
+    nreq = 300
+    tree = KVTree.synthetic([-1] + [0] * nreq, [2000] + [17 + (i * 13) % 90 for i in range(nreq)],
+                            list(range(1, nreq + 1)))
+    q, k, v = make_inputs(nreq, tree.storage_tokens, 32, 8, 128, dtype, seed=41)
+    qd = q.cuda()
+    kp, vp = pack_kv(k.cuda(), v.cuda())
+    p = prepare(schedule(tree, 32, 8, 128, "cube", CostModel.b200()), qd)
+    assert p.layout.num_tc_tasks > 0 and p.layout.num_kn_segs > 3 * 148
+    lse = torch.empty(nreq, 32, device="cuda")
+    first = attention_matrix(qd, kp, vp, p, out_lse=lse).clone()
+    torch.cuda.synchronize()
+    check_status(p)
+    check_against_oracle(q, k, v, tree.paths, first.cpu(), lse.cpu())
+    os.environ["TREE_ATTN_CHECK"] = "0"
+    try:
+        for _ in range(10):
+            attention_matrix(qd, kp, vp, p)
+        torch.cuda.synchronize()
+        assert torch.equal(p.out, first)
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(3):
+                attention_matrix(qd, kp, vp, p)
+        p.out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+    finally:
+        os.environ["TREE_ATTN_CHECK"] = "1"
+    check_status(p)
+    assert torch.equal(p.out, first)
+    assert int(_queue(p).abs().sum().item()) == 0

@@ -4,6 +4,8 @@
 // parameter blocks and launches on the caller's stream: no allocation, no
 // synchronisation, so every call can be captured into a CUDA graph.
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 
 #include "ta_common.cuh"
 #include "ta_kernels.cuh"
@@ -27,6 +29,7 @@ bool layout_ok(const ta_plan_layout* L) {
   if (class_ctas != L->kn_ctas) return false;
   if (L->num_kn_tasks > 0 && (L->kn_ctas < 1 || L->num_kn_segs < 1)) return false;
   if ((L->off_kn_tasks & 3) || (L->off_kn_segs & 3) || (L->off_tc_tasks & 3)) return false;   // int4 loads
+  if (L->off_queue < 0) return false;
   const int32_t* e = L->small_class_end;
   if (e[0] < 0 || e[1] < e[0] || e[2] < e[1] || e[2] != L->num_small_tasks) return false;
   return true;
@@ -41,6 +44,111 @@ bool heads_ok(int32_t hq, int32_t hk, int32_t d, int32_t dtype) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int launch_status(cudaError_t err) { return err == cudaSuccess ? TA_OK : TA_ERR_LAUNCH; }
+
+MergeParams merge_params(const ta_plan_layout* plan, const int32_t* meta, const float* part, const float* lse,
+                         void* out, float* out_lse, int32_t num_q_heads, int32_t num_kv_heads, int32_t* status) {
+  MergeParams p{};
+  p.part = part;
+  p.lse = lse;
+  p.cslots = meta + plan->off_cslots;
+  p.counts = meta + plan->off_pcounts;
+  p.out = out;
+  p.out_lse = out_lse;
+  p.status = status;
+  p.num_requests = plan->num_requests;
+  p.max_slots = plan->max_pslots;
+  p.num_partials = plan->num_partials;
+  p.num_q_heads = num_q_heads;
+  p.group = num_q_heads / num_kv_heads;
+  return p;
+}
+
+// Small-group segments (kn_segs) run on the keys-in-lanes tcgen05 kernel;
+// TREE_ATTN_SMALL_KERNEL=stream selects the streaming warp kernel instead.
+bool use_stream_kernel() {
+  static const bool stream = [] {
+    const char* v = std::getenv("TREE_ATTN_SMALL_KERNEL");
+    return v && std::strcmp(v, "stream") == 0;
+  }();
+  return stream;
+}
+
+// The segment launches of a step.  With `fuse` (ta_attention) the LSE merge
+// runs as the last phase of the small-group kernel when that kernel is the
+// step's last launch; *merged tells the caller whether it did.
+int run_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, const void* kpool,
+                const void* vpool, int64_t pool_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                int32_t head_dim, int32_t dtype, float* part, float* lse, int32_t* status, void* stream,
+                const MergeParams* fuse, bool* merged) {
+  if (merged) *merged = false;
+  if (!layout_ok(plan) || !meta || pool_tokens < 0) return TA_ERR_ARG;
+  if (!heads_ok(num_q_heads, num_kv_heads, head_dim, dtype)) return TA_ERR_UNSUPPORTED;
+  const int tasks = plan->num_small_tasks + plan->num_tc_tasks + plan->num_kn_tasks;
+  if (tasks == 0) return TA_OK;
+  if (!q || !kpool || !vpool || !part || !lse) return TA_ERR_ARG;
+  // bulk copies and TMA need 16-byte aligned bases; rows are 2*head_dim bytes
+  if (!aligned16(meta) || !aligned16(q) || !aligned16(kpool) || !aligned16(vpool) || !aligned16(part)) return TA_ERR_ARG;
+  if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && head_dim != 128) return TA_ERR_UNSUPPORTED;
+  const bool stream_small = use_stream_kernel();
+  // keys-in-lanes kernels are built for tasks of up to 8 query rows
+  if (!stream_small && (plan->kn_class_ctas[2] > 0 || plan->kn_class_ctas[3] > 0 || plan->kn_class_ctas[4] > 0))
+    return TA_ERR_UNSUPPORTED;
+  // TMA coordinates are 32-bit
+  if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && pool_tokens > int64_t(INT32_MAX) - 512) return TA_ERR_ARG;
+
+  SegParams p{};
+  p.q = static_cast<const uint16_t*>(q);
+  p.k = static_cast<const uint16_t*>(kpool);
+  p.v = static_cast<const uint16_t*>(vpool);
+  p.part = part;
+  p.lse = lse;
+  p.qids = meta + plan->off_qids;
+  p.kstart = meta + plan->off_kstart;
+  p.qlen = meta + plan->off_qlen;
+  p.klen = meta + plan->off_klen;
+  p.pieces = meta + plan->off_pieces;
+  p.small_tasks = meta + plan->off_small_tasks;
+  p.tc_tasks = meta + plan->off_tc_tasks;
+  p.kn_offsets = meta + plan->off_kn_offsets;
+  p.kn_tasks = meta + plan->off_kn_tasks;
+  p.kn_segs = meta + plan->off_kn_segs;
+  // the work-queue counters are device scratch inside the metadata buffer
+  p.queue = const_cast<int32_t*>(meta) + plan->off_queue;
+  p.status = status;
+  p.pool_tokens = pool_tokens;
+  p.num_jobs = plan->num_jobs;
+  p.num_pieces = plan->num_pieces;
+  p.max_requests = plan->max_requests;
+  p.kstart_stride = plan->kstart_stride;
+  p.num_requests = plan->num_requests;
+  p.num_partials = plan->num_partials;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.group = num_q_heads / num_kv_heads;
+  p.num_kn_tasks = plan->num_kn_tasks;
+  p.num_kn_segs = plan->num_kn_segs;
+  p.kn_ctas = plan->kn_ctas;
+  p.scale_log2 = kLog2e / std::sqrt(float(head_dim));
+  p.gmul = (65536u + uint32_t(p.group) - 1u) / uint32_t(p.group);
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err = cudaSuccess;
+  if (plan->num_tc_tasks > 0) err = launch_seg_tc(p, plan->num_tc_tasks, dtype, s);
+  p.kn_after_tc = plan->num_tc_tasks > 0 && err == cudaSuccess;
+  if (err == cudaSuccess && plan->num_kn_tasks > 0) {
+    if (stream_small) {
+      // the merge can be fused only when nothing launches after this kernel
+      const bool fuse_here = fuse && plan->num_small_tasks == 0 && plan->num_requests > 0;
+      err = launch_seg_stream(p, fuse_here ? fuse : nullptr, dtype, s);
+      if (err == cudaSuccess && fuse_here && merged) *merged = true;
+    } else {
+      err = launch_seg_kn(p, plan->kn_class_ctas, dtype, s);
+    }
+  }
+  if (err == cudaSuccess && plan->num_small_tasks > 0)
+    err = launch_seg_simt(p, plan->small_class_end, plan->small_max_keys, head_dim, dtype, s);
+  return launch_status(err);
+}
 
 }  // namespace
 
@@ -64,60 +172,8 @@ const char* ta_error_string(int code) {
 int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, const void* kpool,
                const void* vpool, int64_t pool_tokens, int32_t num_q_heads, int32_t num_kv_heads,
                int32_t head_dim, int32_t dtype, float* part, float* lse, int32_t* status, void* stream) {
-  if (!layout_ok(plan) || !meta || pool_tokens < 0) return TA_ERR_ARG;
-  if (!heads_ok(num_q_heads, num_kv_heads, head_dim, dtype)) return TA_ERR_UNSUPPORTED;
-  const int tasks = plan->num_small_tasks + plan->num_tc_tasks + plan->num_kn_tasks;
-  if (tasks == 0) return TA_OK;
-  if (!q || !kpool || !vpool || !part || !lse) return TA_ERR_ARG;
-  // bulk copies and TMA need 16-byte aligned bases; rows are 2*head_dim bytes
-  if (!aligned16(meta) || !aligned16(q) || !aligned16(kpool) || !aligned16(vpool) || !aligned16(part)) return TA_ERR_ARG;
-  if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && head_dim != 128) return TA_ERR_UNSUPPORTED;
-  // keys-in-lanes kernels are built for tasks of up to 8 query rows
-  if (plan->kn_class_ctas[2] > 0 || plan->kn_class_ctas[3] > 0 || plan->kn_class_ctas[4] > 0) return TA_ERR_UNSUPPORTED;
-  // TMA coordinates are 32-bit
-  if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && pool_tokens > int64_t(INT32_MAX) - 512) return TA_ERR_ARG;
-
-  SegParams p{};
-  p.q = static_cast<const uint16_t*>(q);
-  p.k = static_cast<const uint16_t*>(kpool);
-  p.v = static_cast<const uint16_t*>(vpool);
-  p.part = part;
-  p.lse = lse;
-  p.qids = meta + plan->off_qids;
-  p.kstart = meta + plan->off_kstart;
-  p.qlen = meta + plan->off_qlen;
-  p.klen = meta + plan->off_klen;
-  p.pieces = meta + plan->off_pieces;
-  p.small_tasks = meta + plan->off_small_tasks;
-  p.tc_tasks = meta + plan->off_tc_tasks;
-  p.kn_offsets = meta + plan->off_kn_offsets;
-  p.kn_tasks = meta + plan->off_kn_tasks;
-  p.kn_segs = meta + plan->off_kn_segs;
-  p.status = status;
-  p.pool_tokens = pool_tokens;
-  p.num_jobs = plan->num_jobs;
-  p.num_pieces = plan->num_pieces;
-  p.max_requests = plan->max_requests;
-  p.kstart_stride = plan->kstart_stride;
-  p.num_requests = plan->num_requests;
-  p.num_partials = plan->num_partials;
-  p.num_q_heads = num_q_heads;
-  p.num_kv_heads = num_kv_heads;
-  p.group = num_q_heads / num_kv_heads;
-  p.num_kn_tasks = plan->num_kn_tasks;
-  p.num_kn_segs = plan->num_kn_segs;
-  p.kn_ctas = plan->kn_ctas;
-  p.scale_log2 = kLog2e / std::sqrt(float(head_dim));
-  p.gmul = (65536u + uint32_t(p.group) - 1u) / uint32_t(p.group);
-
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t err = cudaSuccess;
-  if (plan->num_tc_tasks > 0) err = launch_seg_tc(p, plan->num_tc_tasks, dtype, s);
-  p.kn_after_tc = plan->num_tc_tasks > 0 && err == cudaSuccess;
-  if (err == cudaSuccess && plan->num_kn_tasks > 0) err = launch_seg_kn(p, plan->kn_class_ctas, dtype, s);
-  if (err == cudaSuccess && plan->num_small_tasks > 0)
-    err = launch_seg_simt(p, plan->small_class_end, plan->small_max_keys, head_dim, dtype, s);
-  return launch_status(err);
+  return run_segment(plan, meta, q, kpool, vpool, pool_tokens, num_q_heads, num_kv_heads, head_dim, dtype, part,
+                     lse, status, stream, nullptr, nullptr);
 }
 
 int ta_merge(const ta_plan_layout* plan, const int32_t* meta, const float* part, const float* lse, void* out,
@@ -127,19 +183,7 @@ int ta_merge(const ta_plan_layout* plan, const int32_t* meta, const float* part,
   if (!heads_ok(num_q_heads, num_kv_heads, head_dim, dtype)) return TA_ERR_UNSUPPORTED;
   if (plan->num_requests == 0) return TA_OK;
   if (!part || !lse || !out || !aligned16(part) || !aligned16(out)) return TA_ERR_ARG;
-  MergeParams p{};
-  p.part = part;
-  p.lse = lse;
-  p.cslots = meta + plan->off_cslots;
-  p.counts = meta + plan->off_pcounts;
-  p.out = out;
-  p.out_lse = out_lse;
-  p.status = status;
-  p.num_requests = plan->num_requests;
-  p.max_slots = plan->max_pslots;
-  p.num_partials = plan->num_partials;
-  p.num_q_heads = num_q_heads;
-  p.group = num_q_heads / num_kv_heads;
+  const MergeParams p = merge_params(plan, meta, part, lse, out, out_lse, num_q_heads, num_kv_heads, status);
   return launch_status(launch_merge(p, head_dim, dtype, static_cast<cudaStream_t>(stream)));
 }
 
@@ -147,9 +191,15 @@ int ta_attention(const ta_plan_layout* plan, const int32_t* meta, const void* q,
                  const void* vpool, int64_t pool_tokens, int32_t num_q_heads, int32_t num_kv_heads,
                  int32_t head_dim, int32_t dtype, float* part, float* lse, void* out, float* out_lse,
                  int32_t* status, void* stream) {
-  int rc = ta_segment(plan, meta, q, kpool, vpool, pool_tokens, num_q_heads, num_kv_heads, head_dim, dtype, part,
-                      lse, status, stream);
-  if (rc != TA_OK) return rc;
+  // Validated up front so a rejected merge argument launches nothing.
+  if (!layout_ok(plan) || !meta) return TA_ERR_ARG;
+  if (!heads_ok(num_q_heads, num_kv_heads, head_dim, dtype)) return TA_ERR_UNSUPPORTED;
+  if (plan->num_requests > 0 && (!out || !aligned16(out))) return TA_ERR_ARG;
+  const MergeParams mp = merge_params(plan, meta, part, lse, out, out_lse, num_q_heads, num_kv_heads, status);
+  bool merged = false;
+  int rc = run_segment(plan, meta, q, kpool, vpool, pool_tokens, num_q_heads, num_kv_heads, head_dim, dtype, part,
+                       lse, status, stream, &mp, &merged);
+  if (rc != TA_OK || merged) return rc;
   return ta_merge(plan, meta, part, lse, out, out_lse, num_q_heads, num_kv_heads, head_dim, dtype, status,
                   stream);
 }

@@ -7,6 +7,7 @@
 // independent 16-byte loads (lanes split head_dim), eight rows in flight.
 #include "ta_common.cuh"
 #include "ta_kernels.cuh"
+#include "ta_merge.cuh"
 
 namespace ta {
 
@@ -16,12 +17,10 @@ constexpr int kMergeWarps = 4;
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) {
-  constexpr int DL = D / 32;
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
   const bool active = item < p.num_requests * p.num_q_heads;
   const int request = active ? item / p.num_q_heads : 0, head = active ? item % p.num_q_heads : 0;
-  const int G = p.group, kv_head = head / G, g = head % G;
 
   // The count and the slot list are plan metadata, which no kernel writes: they
   // are loaded before waiting for the segment kernels (slot loads past the
@@ -32,88 +31,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) 
   pdl_wait();                // the segment kernels before this one have completed
   pdl_trigger();             // the next step's query-tile kernel may set up meanwhile (it waits before any data)
   if (!active) return;
-  if (count < 0 || count > p.max_slots) {
-    if (lane == 0) set_status(p.status, TA_ERR_BOUNDS);
-    count = 0;
-  }
-  const int64_t head_rows = int64_t(kv_head) * p.num_partials;
-
-  float acc[DL];
-#pragma unroll
-  for (int e = 0; e < DL; ++e) acc[e] = 0.f;
-  float m = -INFINITY, z = 0.f;
-  // Lane k holds partial k0 + k of each group of 32: its LSE, weight and row.
-  // Groups after the first (more than 32 partials) rescale the running sums.
-  for (int k0 = 0; k0 < count; k0 += 32) {
-    const int k = k0 + lane;
-    float l = -INFINITY;
-    int64_t row = 0;
-    if (k < count) {
-      const int s = k0 == 0 ? pre_slot : slots[k];
-      if (s >= 0 && s < p.num_partials) {
-        row = (head_rows + s) * G + g;
-        l = p.lse[row];
-      } else {
-        set_status(p.status, TA_ERR_BOUNDS);
-      }
-    }
-    const float m_new = fmaxf(m, warp_max(l));
-    if (m_new == -INFINITY) continue;               // nothing but empty partials so far
-    const float scale = fast_exp2((m - m_new) * kLog2e);   // m = -inf gives 0
-    z *= scale;
-#pragma unroll
-    for (int e = 0; e < DL; ++e) acc[e] *= scale;
-    m = m_new;
-    const float w = fast_exp2((l - m) * kLog2e);        // -inf lse gives 0
-    z += warp_sum(w);
-    // every row of the group in flight at once (eight at a time)
-    const int n = min(32, count - k0);
-    for (int j = 0; j < n; j += 8) {
-      float wj[8];
-      float x[8][DL];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int src = min(j + u, n - 1);
-        wj[u] = __shfl_sync(0xffffffffu, w, src);
-        const int64_t rj = __shfl_sync(0xffffffffu, row, src);
-        if (j + u >= n) wj[u] = 0.f;
-        // an empty partial (weight 0) may hold anything: do not read it
-        const float* ptr = p.part + rj * D + lane * DL;
-#pragma unroll
-        for (int e = 0; e < DL; ++e) x[u][e] = 0.f;
-        if (wj[u] != 0.f) {
-          if constexpr (DL == 4) {
-            const float4 v = *reinterpret_cast<const float4*>(ptr);
-            x[u][0] = v.x; x[u][1] = v.y; x[u][2] = v.z; x[u][3] = v.w;
-          } else if constexpr (DL == 2) {
-            const float2 v = *reinterpret_cast<const float2*>(ptr);
-            x[u][0] = v.x; x[u][1] = v.y;
-          } else {
-            x[u][0] = ptr[0];
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-#pragma unroll
-        for (int e = 0; e < DL; ++e) acc[e] = fmaf(wj[u], x[u][e], acc[e]);
-    }
-  }
-  const float inv = z > 0.f ? 1.f / z : 0.f;
-  uint16_t* out = reinterpret_cast<uint16_t*>(p.out) + (int64_t(request) * p.num_q_heads + head) * D + lane * DL;
-  if constexpr (DL == 4) {
-    uint2 bits;
-    bits.x = Elem<T>::pack2(acc[0] * inv, acc[1] * inv);
-    bits.y = Elem<T>::pack2(acc[2] * inv, acc[3] * inv);
-    *reinterpret_cast<uint2*>(out) = bits;
-  } else if constexpr (DL == 2) {
-    *reinterpret_cast<uint32_t*>(out) = Elem<T>::pack2(acc[0] * inv, acc[1] * inv);
-  } else {
-    *out = Elem<T>::from_float(acc[0] * inv);
-  }
-  if (p.out_lse && lane == 0) {
-    p.out_lse[int64_t(request) * p.num_q_heads + head] = z > 0.f ? m + fast_log2(z) * kLn2 : -INFINITY;
-  }
+  merge_one<T, D>(p, request, head, count, pre_slot, lane);
 }
 
 // Requests with many partials (a plan whose long segments were cut into many

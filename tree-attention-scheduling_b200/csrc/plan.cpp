@@ -32,6 +32,7 @@ constexpr int kKnBox = 32;          // packed segments start on 32-key boundarie
 constexpr int kKnPackRows = 8;      // query rows of a packed tile
 constexpr int kKnPackSegs = 4;      // segments of a packed tile
 constexpr int kGrowingBit = 30;
+constexpr int64_t kQueueWords = 4;  // work-queue counters of the small-group kernel (zero-initialised)
 
 enum Route { kSimt, kKn, kTc };
 
@@ -57,7 +58,8 @@ struct Item {
 };
 
 // Execution pieces: kn jobs cut so no piece holds more than about half a CTA's
-// share of all key tiles; query-tile jobs cut while their CTAs fit one wave.
+// share of all key tiles; query-tile jobs cut a whole level of the longest
+// pieces at a time while their CTAs fit one wave.
 void split_pieces(int njobs, const std::vector<int>& rows, const std::vector<int>& route,
                   const int32_t* keys, const std::vector<char>& splittable, int heads, int sms,
                   std::vector<PieceRec>& pieces) {
@@ -85,23 +87,22 @@ void split_pieces(int njobs, const std::vector<int>& rows, const std::vector<int
       any_tc = true;
     }
   while (any_tc) {
-    // the first job (in order) with the most key tiles per piece among those
-    // that may take one more piece
-    int best = -1;
-    double best_key = 0.0;
-    for (int i = 0; i < njobs; ++i) {
-      if (route[i] != kTc || !splittable[i]) continue;
-      const double t = double(tiles_of(keys[i]));
-      if (!(t / double(count[i] + 1) >= 2.0) || ctas + pairs[i] > sms) continue;
-      const double key = t / double(count[i]);
-      if (best < 0 || key > best_key) {
-        best = i;
-        best_key = key;
-      }
+    // one level: every query-tile job whose pieces are the longest takes one
+    // more piece, if all of them can and the CTAs still fit one wave
+    int64_t longest = 0;
+    for (int i = 0; i < njobs; ++i)
+      if (route[i] == kTc) longest = std::max(longest, cdiv(tiles_of(keys[i]), count[i]));
+    bool ok = true;
+    int64_t extra = 0;
+    for (int i = 0; i < njobs && ok; ++i) {
+      if (route[i] != kTc || cdiv(tiles_of(keys[i]), count[i]) != longest) continue;
+      ok = splittable[i] && double(tiles_of(keys[i])) / double(count[i] + 1) >= 2.0;
+      extra += pairs[i];
     }
-    if (best < 0) break;
-    count[best] += 1;
-    ctas += pairs[best];
+    if (!ok || ctas + extra > sms) break;
+    for (int i = 0; i < njobs; ++i)
+      if (route[i] == kTc && cdiv(tiles_of(keys[i]), count[i]) == longest) count[i] += 1;
+    ctas += extra;
   }
   for (int i = 0; i < njobs; ++i) {
     const int per = int(cdiv(tiles_of(keys[i]), count[i])) * kKeyTile;
@@ -323,14 +324,14 @@ extern "C" int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_
   }
 
   // ---- layout: the arrays in order, each on a 4-int32 boundary ----
-  const int64_t sizes[14] = {int64_t(njobs) * maxr, njobs, njobs, njobs, int64_t(nreq) * maxs, nreq,
+  const int64_t sizes[15] = {int64_t(njobs) * maxr, njobs, njobs, njobs, int64_t(nreq) * maxs, nreq,
                              int64_t(npieces) * 4, nreq, int64_t(nreq) * maxp,
                              int64_t(small[0].size() + small[1].size() + small[2].size()) * 2,
                              int64_t(tc.size()), int64_t(kn_offsets.size()), int64_t(kn_tasks.size()),
-                             int64_t(segs.size())};
-  int64_t offs[14];
+                             int64_t(segs.size()), kQueueWords};
+  int64_t offs[15];
   int64_t total = 0;
-  for (int a = 0; a < 14; ++a) {
+  for (int a = 0; a < 15; ++a) {
     total += (4 - total % 4) % 4;
     offs[a] = total;
     total += sizes[a];
@@ -357,11 +358,11 @@ extern "C" int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_
   L.small_class_end[2] = L.num_small_tasks;
   L.small_max_keys = small_max_keys;
   L.kstart_stride = 1;
-  int32_t* const off_fields[14] = {&L.off_qids, &L.off_kstart, &L.off_qlen, &L.off_klen, &L.off_slots,
+  int32_t* const off_fields[15] = {&L.off_qids, &L.off_kstart, &L.off_qlen, &L.off_klen, &L.off_slots,
                                    &L.off_counts, &L.off_pieces, &L.off_pcounts, &L.off_cslots,
                                    &L.off_small_tasks, &L.off_tc_tasks, &L.off_kn_offsets, &L.off_kn_tasks,
-                                   &L.off_kn_segs};
-  for (int a = 0; a < 14; ++a) *off_fields[a] = int32_t(offs[a]);
+                                   &L.off_kn_segs, &L.off_queue};
+  for (int a = 0; a < 15; ++a) *off_fields[a] = int32_t(offs[a]);
   *layout = L;
   if (!meta || meta_capacity < total) return TA_ERR_TOO_LARGE;
 
@@ -411,5 +412,6 @@ extern "C" int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_
   std::copy(kn_offsets.begin(), kn_offsets.end(), meta + offs[11]);
   std::copy(kn_tasks.begin(), kn_tasks.end(), meta + offs[12]);
   std::copy(segs.begin(), segs.end(), meta + offs[13]);
+  // queue (offs[14]) stays zero
   return TA_OK;
 }

@@ -66,6 +66,7 @@ constexpr uint32_t kHalfBytes = kTileBytes / 2;         // one 64-column swizzle
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;              // + tile * 128
 constexpr float kRescaleThreshold = 8.0f;               // log2 units
+constexpr int kPolyPairs = 1;                           // of every 8 exp2 pairs, this many by polynomial (rest SFU)
 
 struct TcSmem {
   static constexpr uint32_t off_q = 0;                                 // Q_A, Q_B
@@ -192,6 +193,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&bars[V_TAIL], 1);
     fence_barrier_init();
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+    if (tma_q) prefetch_tensormap(&tmap_q);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -231,6 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       unsigned char* ring = smem + (is_k ? TcSmem::off_k : TcSmem::off_v);
       uint64_t* full = &bars[is_k ? K_FULL : V_FULL];
       uint64_t* empty = &bars[is_k ? K_EMPTY : V_EMPTY];
+      const uint64_t policy = l2_evict_first_policy();   // a K/V tile is read by this CTA only
       if (is_k && tma_q) {
         for (int t = 0; t < ntile; ++t) {
           unsigned char* qs = smem + TcSmem::off_q + t * kTileBytes;
@@ -257,8 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int y = int(k0) + j * kKeys;
         unsigned char* dst = ring + st * kTileBytes;
         mbar_arrive_expect_tx(&full[st], kTileBytes);
-        tma_load_3d(dst, map, 0, y, head, &full[st]);
-        tma_load_3d(dst + kHalfBytes, map, 64, y, head, &full[st]);
+        tma_load_3d_hint(dst, map, 0, y, head, &full[st], policy);
+        tma_load_3d_hint(dst + kHalfBytes, map, 64, y, head, &full[st], policy);
       }
     }
     if (!is_k) {
@@ -447,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             x.f = make_float2(s[32 * h + 2 * i], s[32 * h + 2 * i + 1]);
             x = ffma2(x, sc, neg_m);
             F2 e;
-            if ((16 * h + i) % 8 == 7) {    // every eighth pair on the FMA pipe, the rest on the SFU
+            if ((16 * h + i) % 8 >= 8 - kPolyPairs) {   // kPolyPairs of every eight pairs on the FMA pipe
               e = poly_exp2x2(x);
             } else {
               e.f = make_float2(fast_exp2(x.f.x), fast_exp2(x.f.y));

@@ -164,6 +164,11 @@ __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+// Prefetch `bytes` (a multiple of 16) of global memory at `src` into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // L2 policy that marks lines for early eviction (data read once).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t policy;
@@ -179,6 +184,21 @@ __device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* m
       "{%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
       : "memory");
+}
+
+// Tiled 4-D TMA load with an L2 cache-policy hint (a make_pool_map_halves map).
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                                 uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+      "{%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
+      : "memory");
+}
+
+// Bring a tensor map (a __grid_constant__ kernel parameter) into the descriptor cache.
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 // 16-byte global -> shared copy (L2 only) tracked by the thread's cp.async group.
@@ -256,6 +276,24 @@ inline bool make_pool_map(CUtensorMap* map, const void* base, int64_t tokens, in
   cuuint32_t box[3] = {64, cuuint32_t(box_rows), 1};
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// The same pool [heads, tokens, 128] as a 4-D map whose two 64-column halves
+// are a dimension of their own (dims: 64 columns, tokens, 2 halves, heads):
+// one box of box_rows tokens x both halves lands exactly like two 64-column
+// boxes placed one after the other (half-major, 128-byte swizzle), so a
+// 128-column tile of K or V needs one TMA instruction instead of two.
+inline bool make_pool_map_halves(CUtensorMap* map, const void* base, int64_t tokens, int heads, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || tokens <= 0 || heads <= 0) return false;
+  cuuint64_t dims[4] = {64, cuuint64_t(tokens), 2, cuuint64_t(heads)};
+  cuuint64_t strides[3] = {128 * 2, 64 * 2, cuuint64_t(tokens) * 128 * 2};
+  cuuint32_t box[4] = {64, cuuint32_t(box_rows), 2, 1};
+  cuuint32_t elem[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(base), dims, strides, box, elem,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;

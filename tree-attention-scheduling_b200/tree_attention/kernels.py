@@ -115,7 +115,8 @@ def split_pieces(jobs, groups, heads, use_tc, sms, no_split_from=None):
     jobs, so splitting changes the work distribution, never the result beyond
     float rounding.  Keys-in-lanes jobs are cut so no piece holds more than
     about half a CTA's share of all key tiles; query-tile jobs are cut while
-    their CTAs still fit one wave on ``sms`` SMs.  Jobs whose first position is
+    their CTAs still fit one wave on ``sms`` SMs, a whole level of the longest
+    pieces at a time.  Jobs whose first position is
     at or past ``no_split_from`` (the growing decode tails) stay whole.
     """
     n = len(jobs)
@@ -135,16 +136,24 @@ def split_pieces(jobs, groups, heads, use_tc, sms, no_split_from=None):
 
     tc = [i for i in range(n) if route[i] == "tc"]
     if tc:
+        # Cut level by level: every job whose pieces are the longest takes one
+        # more piece, as long as all of them can and the query-tile CTAs still
+        # fit one wave.  A partial level would add CTAs without shortening the
+        # longest piece; the SMs it leaves free run the small-group kernel
+        # beside the query-tile kernel.
         pairs = {i: -(-rows[i] // TC_ROWS) * heads for i in tc}
         ctas = sum(pairs.values())
         while True:
-            best = max((i for i in tc if splittable[i] and _tiles(keys[i]) / (count[i] + 1) >= 2
-                        and ctas + pairs[i] <= sms),
-                       key=lambda i: _tiles(keys[i]) / count[i], default=None)
-            if best is None:
+            longest = max(-(-_tiles(keys[i]) // count[i]) for i in tc)
+            level = [i for i in tc if -(-_tiles(keys[i]) // count[i]) == longest]
+            if not all(splittable[i] and _tiles(keys[i]) / (count[i] + 1) >= 2 for i in level):
                 break
-            count[best] += 1
-            ctas += pairs[best]
+            extra = sum(pairs[i] for i in level)
+            if ctas + extra > sms:
+                break
+            for i in level:
+                count[i] += 1
+            ctas += extra
 
     pieces = []
     for i in range(n):
@@ -357,13 +366,16 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
     kn_segs = np.array(segs, dtype=np.int32).reshape(-1, 12)
     return dict(qids=qids, kids=kids, qlen=qlen, klen=klen, slots=slots, counts=counts,
                 pieces=pieces, pcounts=pcounts, cslots=cslots, small_tasks=small_tasks, tc_tasks=tc_tasks,
-                kn_offsets=kn_offsets, kn_tasks=kn_tasks, kn_segs=kn_segs, small_class_end=class_end,
+                kn_offsets=kn_offsets, kn_tasks=kn_tasks, kn_segs=kn_segs,
+                queue=np.zeros(QUEUE_WORDS, dtype=np.int32), small_class_end=class_end,
                 small_max_keys=small_max_keys, kn_ctas=kn_ctas, kn_class_ctas=kn_class_ctas, contiguous_k=contiguous_k,
                 num_partials=slot)
 
 
 _ORDER = ("qids", "kids", "qlen", "klen", "slots", "counts", "pieces", "pcounts", "cslots", "small_tasks",
-          "tc_tasks", "kn_offsets", "kn_tasks", "kn_segs")
+          "tc_tasks", "kn_offsets", "kn_tasks", "kn_segs", "queue")
+# Work-queue counters of the small-group kernel (zero between calls).
+QUEUE_WORDS = 4
 
 
 def _sm_count(device):
@@ -379,7 +391,8 @@ _SHAPES = {
     "pieces": lambda L: (L.num_pieces, 4), "pcounts": lambda L: (L.num_requests,),
     "cslots": lambda L: (L.num_requests, L.max_pslots), "small_tasks": lambda L: (L.num_small_tasks, 2),
     "tc_tasks": lambda L: (L.num_tc_tasks, 4), "kn_offsets": lambda L: (L.kn_ctas + 1,),
-    "kn_tasks": lambda L: (L.num_kn_tasks, 4), "kn_segs": lambda L: (L.num_kn_segs, 12)}
+    "kn_tasks": lambda L: (L.num_kn_tasks, 4), "kn_segs": lambda L: (L.num_kn_segs, 12),
+    "queue": lambda L: (QUEUE_WORDS,)}
 _OFFSET_FIELD = {name: "off_" + ("kstart" if name == "kids" else name) for name in _ORDER}
 
 
