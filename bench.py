@@ -59,6 +59,9 @@ NREQ, ROOT_LEN, LEAF_LEN = 128, 8128, 64
 HQ, HK, D = 32, 8, 128
 SEED = 101
 COPIES = 4
+E2E_STEPS = 200          # steps per replay of the end-to-end loop
+E2E_REPLAYS = 5          # replays timed; the median is reported
+GRID_STEPS = 5           # steps per shape of the default line's grid summary
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
@@ -212,11 +215,8 @@ class Step:
         self.lib = _lib.load()
         L = prepared.layout
         small = sum(1 for i, e in enumerate(L.small_class_end) if e > (L.small_class_end[i - 1] if i else 0))
-        if os.environ.get("TREE_ATTN_SMALL_KERNEL") != "stream":
-            kn, fused = sum(1 for c in range(5) if L.kn_class_ctas[c] > 0), False
-        else:   # one small-group launch, which also merges when it is the step's last launch
-            kn, fused = (1 if L.num_kn_segs else 0), L.num_kn_segs > 0 and small == 0
-        self.launches = small + (1 if L.num_tc_tasks else 0) + kn + (0 if fused else 1)
+        kn = sum(1 for c in range(5) if L.kn_class_ctas[c] > 0)
+        self.launches = small + (1 if L.num_tc_tasks else 0) + kn + 1          # + the merge
 
     def attention(self, copy=0):
         """The whole step through the public C entry point ta_attention."""
@@ -293,8 +293,9 @@ def time_e2e(q_host, plans, copies, steps, warmup, world):
     copy of step i-1 overlap step i's attention.  Two plan objects alternate, so an output buffer is not
     rewritten before its copy to the host has finished.  The loop of K steps is timed twice: issued
     eagerly from Python, and recorded once into a CUDA graph and replayed (the serving-loop form: the
-    Python work per step leaves the timed region, the copies and kernels stay).
-    Returns (graph us per step, eager us per step, H2D bytes, D2H bytes)."""
+    Python work per step leaves the timed region, the copies and kernels stay).  The graph holds
+    ``steps`` steps (at least E2E_STEPS) and is replayed E2E_REPLAYS times; the median replay is the
+    figure.  Also returns each copy's time on its own."""
     n = len(copies)
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
     out_host = [torch.empty(p.out.shape, dtype=p.out.dtype, pin_memory=True) for p in plans]
@@ -342,11 +343,19 @@ def time_e2e(q_host, plans, copies, steps, warmup, world):
     run(warmup)
     eager_us = timed(lambda: run(steps))
     graph = capture(lambda: run(steps))
-    for _ in range(max(1, warmup // steps)):
-        graph.replay()
-    graph_us = timed(graph.replay)
+    graph.replay()
+    replays = sorted(timed(graph.replay) for _ in range(E2E_REPLAYS))
+    graph_us = replays[len(replays) // 2]
     del graph
-    return graph_us, eager_us, q_host.numel() * q_host.element_size(), out_host[0].numel() * out_host[0].element_size()
+    # one 1 MiB copy each way on its own: what the pipeline has to hide behind the kernels
+    copy_us = []
+    for dst, src in ((copies[0][0], q_host), (out_host[0], plans[0].out)):
+        for _ in range(3):
+            dst.copy_(src, non_blocking=True)
+        copy_us.append(timed(lambda: [dst.copy_(src, non_blocking=True) for _ in range(steps)]))
+    sizes = (q_host.numel() * q_host.element_size(), out_host[0].numel() * out_host[0].element_size())
+    return dict(graph_us=graph_us, graph_replays_us=[round(x, 3) for x in replays], eager_us=eager_us,
+                h2d_bytes=sizes[0], d2h_bytes=sizes[1], h2d_copy_us=copy_us[0], d2h_copy_us=copy_us[1])
 
 
 def cpu_oracle_step_us(tree, plan, q, kp, vp, budget_s=10.0, max_steps=200):
@@ -411,12 +420,13 @@ def run_b200(args):
 
     q_host = q.cpu().pin_memory()
     second = kernels.prepare(plan, q, num_kv_heads=len(heads))
-    e2e_us, e2e_eager_us, h2d, d2h = time_e2e(q_host, [prepared, second], copies, max(3, args.steps),
-                                              args.warmup, world)
-    e2e_eager_us = max_over_ranks(e2e_eager_us, world)
+    e2e = time_e2e(q_host, [prepared, second], copies, 20 if args.quick else max(E2E_STEPS, args.steps),
+                   args.warmup, world)
+    e2e_eager_us = max_over_ranks(e2e["eager_us"], world)
     kernels.check_status(second)
     del second
-    e2e_us = max_over_ranks(e2e_us, world)
+    e2e_us = max_over_ranks(e2e["graph_us"], world)
+    h2d, d2h = e2e["h2d_bytes"], e2e["d2h_bytes"]
     kernels.check_status(prepared)
 
     total_bytes = kv_bytes(tree)                     # all ranks together
@@ -442,9 +452,10 @@ def run_b200(args):
         "e2e": {"value": round(total_bytes / (e2e_us * 1e-6) / 1e9, 2), "unit": "GB/s", "step_us": round(e2e_us, 3),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "kernels.attention_matrix per step with pinned host Q in and output out, steps pipelined "
-                        "over three streams (H2D of step i+1 and D2H of step i-1 overlap step i); the K-step loop "
-                        "recorded once as a CUDA graph and replayed",
-                "eager_step_us": round(e2e_eager_us, 3)},
+                        "over three streams (H2D of step i+1 and D2H of step i-1 overlap step i); the loop of "
+                        f"{E2E_STEPS} steps recorded once as a CUDA graph, median of {E2E_REPLAYS} replays",
+                "replays_us": e2e["graph_replays_us"], "eager_step_us": round(e2e_eager_us, 3),
+                "h2d_copy_us": round(e2e["h2d_copy_us"], 2), "d2h_copy_us": round(e2e["d2h_copy_us"], 2)},
         "gpu_launches": step.launches * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": rank_traffic(len(heads)),
@@ -464,6 +475,22 @@ def run_b200(args):
                                 "step_us": round(cpu_us, 1), "cores": threads, "kind": "port",
                                 "sample": f"{n} full headline steps of the FP32 plan-driven oracle "
                                           f"(oracle/attention.py segmented_attention, same cube plan)"}
+    if world == 1 and not (args.quick or args.no_extras):
+        # the other BASELINE configurations, compactly: configs[2] (every grid shape, few steps) and
+        # configs[3] (the cube plan reused vs rebuilt)
+        geo, rows = grid_summary(GRID_STEPS, 3)
+        speedups = [r["speedup"] for r in rows]
+        line["grid"] = {"geomean_speedup": round(geo, 4), "min": min(speedups), "max": max(speedups),
+                        "shapes": len(rows), "steps": GRID_STEPS, "target": 1.3,
+                        "what": "configs[2]: tree (cube) plan vs per-request plan on the same kernels"}
+        rows = {r["mode"]: r for r in decode_summary(("cube",))}
+        line["decode_reuse"] = {"cached_step_us": rows["cached"]["per_step_us"],
+                                "rebuilt_step_us": rows["rebuild"]["per_step_us"],
+                                "cached_attention_us": rows["cached"]["attention_us"],
+                                "cached_planning_us": rows["cached"]["planning_us"],
+                                "rebuilt_planning_us": rows["rebuild"]["planning_us"],
+                                "max_rel_l2": max(rows["cached"]["max_rel_l2"], rows["rebuild"]["max_rel_l2"]),
+                                "what": "configs[3], cube plan: planning + attention per decode step"}
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -542,14 +569,14 @@ def random_inputs(tree, nreq, device, seed, copies=1):
     return out
 
 
-def run_grid(args):
-    """configs[2]: 81 seeded shapes, tree plan vs per-request plan on the same kernels."""
+def grid_summary(steps, warmup, seed=201):
+    """every shape of the 81-shape evaluation grid, tree (cube) plan vs per-request plan on the
+    same kernels.  Returns (geomean speed-up, rows)."""
     from tree_attention import workloads
     import math
-    torch.cuda.set_device(0)
     model = CostModel.b200()
     rows = []
-    for params, tree in workloads.evaluation_grid(seed=args.seed or 201):
+    for params, tree in workloads.evaluation_grid(seed=seed):
         nreq = len(tree.paths)
         kvb = kv_bytes(tree)
         copies = max(1, min(8, math.ceil((256 << 20) / kvb)))
@@ -561,7 +588,7 @@ def run_grid(args):
             plan_us = (time.perf_counter() - t0) * 1e6
             prepared = kernels.prepare(plan, inputs[0][0])
             step = Step(inputs, prepared)
-            whole, _, _ = time_step(step, args.steps, args.warmup, 1)
+            whole, _, _ = time_step(step, steps, warmup, 1)
             kernels.check_status(prepared)
             row[method] = dict(step_us=round(whole, 2), plan_us=round(plan_us, 1), jobs=len(prepared.jobs))
             del prepared, step
@@ -570,7 +597,14 @@ def run_grid(args):
         del inputs
         torch.cuda.empty_cache()
     speedups = [r["speedup"] for r in rows]
-    geo = math.exp(sum(math.log(x) for x in speedups) / len(speedups))
+    return math.exp(sum(math.log(x) for x in speedups) / len(speedups)), rows
+
+
+def run_grid(args):
+    """configs[2]: 81 seeded shapes, tree plan vs per-request plan on the same kernels."""
+    torch.cuda.set_device(0)
+    geo, rows = grid_summary(args.steps, args.warmup, args.seed or 201)
+    speedups = [r["speedup"] for r in rows]
     line = {"config": "grid (configs[2]): 81 shapes, requests {16,64,256} x depth {1,2,4} x shared "
                       "{0.25,0.75,0.99} x branching {2,4,16}, context 2048-16384",
             "metric": "geomean speed-up of the tree (cube) plan over the per-request plan, same kernels",
@@ -695,13 +729,14 @@ def run_qwen(args):
         print(json.dumps(line), flush=True)
 
 
-def run_decode(args):
-    """configs[3]: a 32-request 2-level tree, 16 decode steps, plan reused vs rebuilt."""
+def decode_summary(methods=("fixed", "greedy", "cube")):
+    """a 32-request 2-level tree, 16 decode steps of one token per request; the plan built once
+    at prompt time and reused (CachedDecodePlan) vs rebuilt every step.  One row per (method, mode) with
+    planning + attention per step; the first and last steps are checked against the FP32 oracle."""
     from tree_attention import workloads
     from tree_attention.kernels import CachedDecodePlan
     from oracle import attention as oracle
     import copy as _copy
-    torch.cuda.set_device(0)
     steps = 16
     base = workloads.decode_tree()
     prefix = base.storage_tokens
@@ -731,7 +766,7 @@ def run_decode(args):
             raise AssertionError(f"decode step {step}: rel L2 {err:.3e}")
         return err
 
-    for method in ("fixed", "greedy", "cube"):
+    for method in methods:
         for mode in ("rebuild", "cached"):
             tree = _copy.deepcopy(base)
             leaves = list(range(len(base.nodes) - nreq, len(base.nodes)))
@@ -764,9 +799,15 @@ def run_decode(args):
                                 per_step_us=round(sum(total) / steps, 1),
                                 amortized_us=round((initial_us + sum(total)) / steps, 1),
                                 max_rel_l2=worst))
+    return results
+
+
+def run_decode(args):
+    """configs[3]: a 32-request 2-level tree, 16 decode steps, plan reused vs rebuilt."""
+    torch.cuda.set_device(0)
     line = {"config": "decode (configs[3]): 32 requests, 4096-token root, 4 x 1024 branches, 32 x 256 leaves, "
                       "16 steps of 1 token per request", "metric": "planning + attention per step (us)",
-            "cost_model": "CostModel.b200()", "results": results}
+            "cost_model": "CostModel.b200()", "results": decode_summary()}
     print(json.dumps(line), flush=True)
 
 
@@ -779,6 +820,7 @@ def main():
     ap.add_argument("--method", default="cube", choices=["request", "fixed", "greedy", "cube"])
     ap.add_argument("--all-plans", action="store_true", help="also time the fixed and greedy plans")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the grid and decode-reuse summaries")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--burn-s", type=float, default=1.0, help="sustained untimed load before timing (clocks)")
     ap.add_argument("--config", choices=["headline", "grid", "decode", "calibrate", "qwen"], default="headline")

@@ -52,13 +52,7 @@
  *                                           within its job (a job's rows may be cut into
  *                                           several segments), 0, 0; a task of several
  *                                           segments is one 128-key tile
- *   queue       [4]                         work-queue counters of the small-group kernel;
- *                                           zero when the plan is built, written by the
- *                                           kernels of a call and zero again when it
- *                                           completes (calls on one plan must not overlap)
- * Every array starts at a multiple of 4 int32 (16 bytes).  The metadata buffer
- * is therefore not read-only: klen (decode plans) and queue are written on the
- * device.  Partial slot s of a
+ * Every array starts at a multiple of 4 int32 (16 bytes).  Partial slot s of a
  * piece holds query rows s*G .. s*G+G-1 (one request).
  *
  * Return value: 0 on success, otherwise a TA_ERR_* code describing a rejected
@@ -75,7 +69,7 @@
 extern "C" {
 #endif
 
-#define TA_ABI_VERSION 6
+#define TA_ABI_VERSION 5
 
 #define TA_DTYPE_BF16 1
 #define TA_DTYPE_F16 2
@@ -133,7 +127,6 @@ typedef struct ta_plan_layout {
   int32_t off_kn_offsets;
   int32_t off_kn_tasks;
   int32_t off_kn_segs;
-  int32_t off_queue;
 } ta_plan_layout;
 
 /* ABI version of the loaded library (TA_ABI_VERSION). */

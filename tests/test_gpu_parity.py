@@ -417,16 +417,11 @@ def _segment_then_merge(qd, kp, vp, p, lse_out):
     return out
 
 
-def _queue(p):
-    return p.metadata[p.layout.off_queue:p.layout.off_queue + kernels.QUEUE_WORDS]
-
-
 @pytest.mark.parametrize("heads", [(8, 8), (16, 8), (32, 8), (64, 8)], ids=["G1", "G2", "G4", "G8"])
 def test_small_group_kernel_group_sizes(heads):
-    """The small-group kernel with 1, 2, 4 and 8 query heads per KV head: segments of up to 8 query
-    rows cut into four-row items (a request's rows split across items for G = 8, several requests per
-    item for G = 1 and 2), shared small groups and private leaves of 1..200 keys, fused merge and
-    separate merge kernel agreeing, queue counters back at zero after each call."""
+    """The keys-in-lanes kernel with 1, 2, 4 and 8 query heads per KV head: segments of up to 8 query
+    rows (several requests per segment for G = 1 and 2, one request for G = 8), shared small groups and
+    private leaves of 1..200 keys; ta_attention and ta_segment + ta_merge give identical results."""
     hq, hk = heads
     leaves = [1, 7, 16, 33, 64, 65, 127, 200]
     parents = [-1, 0, 0] + [1] * 4 + [2] * 4
@@ -443,20 +438,18 @@ def test_small_group_kernel_group_sizes(heads):
         out = attention_matrix(qd, kp, vp, p, out_lse=lse).clone()
         torch.cuda.synchronize()
         check_status(p)
-        assert int(_queue(p).abs().sum().item()) == 0
         check_against_oracle(q, k, v, tree.paths, out.cpu(), lse.cpu())
         lse2 = torch.empty_like(lse)
         out2 = _segment_then_merge(qd, kp, vp, p, lse2)
         torch.cuda.synchronize()
         check_status(p)
-        assert int(_queue(p).abs().sum().item()) == 0
         assert torch.equal(out2, out) and torch.equal(lse2, lse)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_small_group_kernel_beside_query_tiles(dtype):
-    """A shared root on the query-tile kernel and 300 private leaves on the small-group kernel, which
-    starts beside it; more segments than resident CTAs, so CTAs take several from the queue.  Ten
+    """A shared root on the query-tile kernel and 300 private leaves on the keys-in-lanes kernel, which
+    is placed on the SMs the query-tile kernel leaves free; more segments than resident CTAs.  Ten
     back-to-back calls and a graph replay of three give the same result as the first call."""
     nreq = 300
     tree = KVTree.synthetic([-1] + [0] * nreq, [2000] + [17 + (i * 13) % 90 for i in range(nreq)],
@@ -490,4 +483,33 @@ def test_small_group_kernel_beside_query_tiles(dtype):
         os.environ["TREE_ATTN_CHECK"] = "1"
     check_status(p)
     assert torch.equal(p.out, first)
-    assert int(_queue(p).abs().sum().item()) == 0
+
+
+def test_bounded_wait_gives_up_and_context_recovers():
+    """A bounded device wait that runs out (the SIMT kernel's test hook makes every CTA wait on a barrier
+    nothing completes) ends the kernel with TA_ERR_TIMEOUT instead of hanging; the context stays usable and
+    the next call on the same plan is correct.  No GPU fault is involved: the wait gives up after about a
+    second, the CTA waits for its own copies in flight and exits."""
+    tree = build_tree(_Lib, SPECS["small_config1"])
+    q, k, v = make_inputs(len(tree.paths), tree.storage_tokens, 8, 2, 64, torch.bfloat16, seed=12)
+    qd = q.cuda()
+    kp, vp = pack_kv(k.cuda(), v.cuda())
+    p = prepare(schedule(tree, 8, 2, 64, "cube", CostModel(kv_split=128)), qd)
+    assert p.layout.num_small_tasks > 0 and p.layout.num_tc_tasks == 0 and p.layout.num_kn_tasks == 0
+    os.environ["TREE_ATTN_CHECK"] = "0"
+    os.environ["TREE_ATTN_TEST_STALL"] = "1"
+    try:
+        attention_matrix(qd, kp, vp, p)
+        torch.cuda.synchronize()
+    finally:
+        os.environ.pop("TREE_ATTN_TEST_STALL", None)
+        os.environ["TREE_ATTN_CHECK"] = "1"
+    code = int(p.status.item())
+    assert code & kernels._lib.ERR_TIMEOUT, code
+    assert not code & kernels._lib.ERR_BOUNDS, code
+    p.status.zero_()
+    lse = torch.empty(len(tree.paths), 8, device="cuda")
+    out = attention_matrix(qd, kp, vp, p, out_lse=lse).cpu()
+    torch.cuda.synchronize()
+    check_status(p)
+    check_against_oracle(q, k, v, tree.paths, out, lse.cpu())

@@ -145,3 +145,53 @@ def test_cached_decoder_graph_generate_gpu():
     graphed.step(graphed.logits.argmax(-1).tolist())
     torch.testing.assert_close(graphed.logits.float(), reference_logits(model, graphed.sequences).float(),
                                atol=4e-3, rtol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cached", [False, True])
+def test_layer_attention_matches_fp32_on_qwen3_4b_shape(cached, monkeypatch):
+    """Layer-level check on the Qwen3-4B attention shape (the reference's scripts/model_checks.py:42-64):
+    every layer's decode-step attention from the B200 kernels is compared with the FP32 oracle on the same
+    queries and pools -- relative L2 of the whole layer output (the reference reports 0.218% at most on
+    Qwen3-4B), at most 5e-3 per (request, query head), and the reference's atol .008 / rtol .03.  Random
+    init N(0, 0.02), hidden 2560, 32 query / 8 KV heads, head_dim 128, four layers; eight requests share a
+    600-token document and end in 16 private tokens each (query-tile and small-group kernels both run)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    torch.manual_seed(401)
+    config = Qwen3Config(vocab_size=2048, hidden_size=2560, intermediate_size=9728, num_hidden_layers=4,
+                         num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1_000_000.0,
+                         rms_norm_eps=1e-6, initializer_range=0.02, attn_implementation="eager")
+    model = Qwen3ForCausalLM(config).to(dtype=torch.bfloat16, device="cuda").eval()
+    g = torch.Generator().manual_seed(401)
+    document = torch.randint(0, config.vocab_size, (600,), generator=g).tolist()
+    sequences = [document + torch.randint(0, config.vocab_size, (16,), generator=g).tolist() for _ in range(8)]
+    cls = qwen.CachedPrefixDecoder if cached else qwen.SharedKVDecoder
+    decoder = cls(model, sequences, max_new_tokens=4, method="cube", cost_model=CostModel.b200())
+    original = qwen.attention_matrix
+    worst = {"layer_rel_l2": 0.0, "head_rel_l2": 0.0, "layers": 0}
+
+    def checked(q, kp, vp, prepared, out_lse=None):
+        actual = original(q, kp, vp, prepared, out_lse)
+        paths = current_paths(decoder)
+        _, reference, _ = oracle.request_attention(q.float().cpu(), kp.permute(1, 0, 2).float().cpu(),
+                                                   vp.permute(1, 0, 2).float().cpu(), paths, return_lse=True)
+        host = actual.float().cpu()
+        error = host - reference
+        layer = (torch.linalg.vector_norm(error) / torch.linalg.vector_norm(reference)).item()
+        heads = (error.norm(dim=-1) / reference.norm(dim=-1)).max().item()
+        worst["layer_rel_l2"] = max(worst["layer_rel_l2"], layer)
+        worst["head_rel_l2"] = max(worst["head_rel_l2"], heads)
+        worst["layers"] += 1
+        torch.testing.assert_close(host, reference.to(actual.dtype).float(), atol=.008, rtol=.03)
+        return actual
+
+    monkeypatch.setattr(qwen, "attention_matrix", checked)
+    for _ in range(3):
+        decoder.step(decoder.logits.argmax(-1).tolist())
+    torch.cuda.synchronize()
+    assert worst["layers"] == 3 * config.num_hidden_layers
+    assert worst["head_rel_l2"] <= 5e-3
+    print(f"\nQwen3-4B-shaped layers ({'cached' if cached else 'rebuilt'} plans): max layer relative L2 "
+          f"{100 * worst['layer_rel_l2']:.4f}% (reference on Qwen3-4B: 0.218%), max per-(request, head) "
+          f"{worst['head_rel_l2']:.2e}")

@@ -29,7 +29,6 @@ bool layout_ok(const ta_plan_layout* L) {
   if (class_ctas != L->kn_ctas) return false;
   if (L->num_kn_tasks > 0 && (L->kn_ctas < 1 || L->num_kn_segs < 1)) return false;
   if ((L->off_kn_tasks & 3) || (L->off_kn_segs & 3) || (L->off_tc_tasks & 3)) return false;   // int4 loads
-  if (L->off_queue < 0) return false;
   const int32_t* e = L->small_class_end;
   if (e[0] < 0 || e[1] < e[0] || e[2] < e[1] || e[2] != L->num_small_tasks) return false;
   return true;
@@ -63,24 +62,10 @@ MergeParams merge_params(const ta_plan_layout* plan, const int32_t* meta, const 
   return p;
 }
 
-// Small-group segments (kn_segs) run on the keys-in-lanes tcgen05 kernel;
-// TREE_ATTN_SMALL_KERNEL=stream selects the streaming warp kernel instead.
-bool use_stream_kernel() {
-  static const bool stream = [] {
-    const char* v = std::getenv("TREE_ATTN_SMALL_KERNEL");
-    return v && std::strcmp(v, "stream") == 0;
-  }();
-  return stream;
-}
-
-// The segment launches of a step.  With `fuse` (ta_attention) the LSE merge
-// runs as the last phase of the small-group kernel when that kernel is the
-// step's last launch; *merged tells the caller whether it did.
+// The segment launches of a step.
 int run_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, const void* kpool,
                 const void* vpool, int64_t pool_tokens, int32_t num_q_heads, int32_t num_kv_heads,
-                int32_t head_dim, int32_t dtype, float* part, float* lse, int32_t* status, void* stream,
-                const MergeParams* fuse, bool* merged) {
-  if (merged) *merged = false;
+                int32_t head_dim, int32_t dtype, float* part, float* lse, int32_t* status, void* stream) {
   if (!layout_ok(plan) || !meta || pool_tokens < 0) return TA_ERR_ARG;
   if (!heads_ok(num_q_heads, num_kv_heads, head_dim, dtype)) return TA_ERR_UNSUPPORTED;
   const int tasks = plan->num_small_tasks + plan->num_tc_tasks + plan->num_kn_tasks;
@@ -89,10 +74,8 @@ int run_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, 
   // bulk copies and TMA need 16-byte aligned bases; rows are 2*head_dim bytes
   if (!aligned16(meta) || !aligned16(q) || !aligned16(kpool) || !aligned16(vpool) || !aligned16(part)) return TA_ERR_ARG;
   if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && head_dim != 128) return TA_ERR_UNSUPPORTED;
-  const bool stream_small = use_stream_kernel();
   // keys-in-lanes kernels are built for tasks of up to 8 query rows
-  if (!stream_small && (plan->kn_class_ctas[2] > 0 || plan->kn_class_ctas[3] > 0 || plan->kn_class_ctas[4] > 0))
-    return TA_ERR_UNSUPPORTED;
+  if (plan->kn_class_ctas[2] > 0 || plan->kn_class_ctas[3] > 0 || plan->kn_class_ctas[4] > 0) return TA_ERR_UNSUPPORTED;
   // TMA coordinates are 32-bit
   if ((plan->num_tc_tasks > 0 || plan->num_kn_tasks > 0) && pool_tokens > int64_t(INT32_MAX) - 512) return TA_ERR_ARG;
 
@@ -112,8 +95,6 @@ int run_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, 
   p.kn_offsets = meta + plan->off_kn_offsets;
   p.kn_tasks = meta + plan->off_kn_tasks;
   p.kn_segs = meta + plan->off_kn_segs;
-  // the work-queue counters are device scratch inside the metadata buffer
-  p.queue = const_cast<int32_t*>(meta) + plan->off_queue;
   p.status = status;
   p.pool_tokens = pool_tokens;
   p.num_jobs = plan->num_jobs;
@@ -135,18 +116,14 @@ int run_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, 
   cudaError_t err = cudaSuccess;
   if (plan->num_tc_tasks > 0) err = launch_seg_tc(p, plan->num_tc_tasks, dtype, s);
   p.kn_after_tc = plan->num_tc_tasks > 0 && err == cudaSuccess;
-  if (err == cudaSuccess && plan->num_kn_tasks > 0) {
-    if (stream_small) {
-      // the merge can be fused only when nothing launches after this kernel
-      const bool fuse_here = fuse && plan->num_small_tasks == 0 && plan->num_requests > 0;
-      err = launch_seg_stream(p, fuse_here ? fuse : nullptr, dtype, s);
-      if (err == cudaSuccess && fuse_here && merged) *merged = true;
-    } else {
-      err = launch_seg_kn(p, plan->kn_class_ctas, dtype, s);
-    }
-  }
-  if (err == cudaSuccess && plan->num_small_tasks > 0)
+  if (err == cudaSuccess && plan->num_kn_tasks > 0) err = launch_seg_kn(p, plan->kn_class_ctas, dtype, s);
+  if (err == cudaSuccess && plan->num_small_tasks > 0) {
+    // Test hook (TREE_ATTN_TEST_STALL=1): the SIMT kernel waits on a barrier
+    // nothing completes, so its bounded waits give up and report TA_ERR_TIMEOUT.
+    const char* stall = std::getenv("TREE_ATTN_TEST_STALL");
+    p.test_stall = stall && std::strcmp(stall, "1") == 0;
     err = launch_seg_simt(p, plan->small_class_end, plan->small_max_keys, head_dim, dtype, s);
+  }
   return launch_status(err);
 }
 
@@ -173,7 +150,7 @@ int ta_segment(const ta_plan_layout* plan, const int32_t* meta, const void* q, c
                const void* vpool, int64_t pool_tokens, int32_t num_q_heads, int32_t num_kv_heads,
                int32_t head_dim, int32_t dtype, float* part, float* lse, int32_t* status, void* stream) {
   return run_segment(plan, meta, q, kpool, vpool, pool_tokens, num_q_heads, num_kv_heads, head_dim, dtype, part,
-                     lse, status, stream, nullptr, nullptr);
+                     lse, status, stream);
 }
 
 int ta_merge(const ta_plan_layout* plan, const int32_t* meta, const float* part, const float* lse, void* out,
@@ -195,11 +172,9 @@ int ta_attention(const ta_plan_layout* plan, const int32_t* meta, const void* q,
   if (!layout_ok(plan) || !meta) return TA_ERR_ARG;
   if (!heads_ok(num_q_heads, num_kv_heads, head_dim, dtype)) return TA_ERR_UNSUPPORTED;
   if (plan->num_requests > 0 && (!out || !aligned16(out))) return TA_ERR_ARG;
-  const MergeParams mp = merge_params(plan, meta, part, lse, out, out_lse, num_q_heads, num_kv_heads, status);
-  bool merged = false;
   int rc = run_segment(plan, meta, q, kpool, vpool, pool_tokens, num_q_heads, num_kv_heads, head_dim, dtype, part,
-                       lse, status, stream, &mp, &merged);
-  if (rc != TA_OK || merged) return rc;
+                       lse, status, stream);
+  if (rc != TA_OK) return rc;
   return ta_merge(plan, meta, part, lse, out, out_lse, num_q_heads, num_kv_heads, head_dim, dtype, status,
                   stream);
 }

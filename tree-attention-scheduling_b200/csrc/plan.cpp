@@ -32,7 +32,6 @@ constexpr int kKnBox = 32;          // packed segments start on 32-key boundarie
 constexpr int kKnPackRows = 8;      // query rows of a packed tile
 constexpr int kKnPackSegs = 4;      // segments of a packed tile
 constexpr int kGrowingBit = 30;
-constexpr int64_t kQueueWords = 4;  // work-queue counters of the small-group kernel (zero-initialised)
 
 enum Route { kSimt, kKn, kTc };
 
@@ -324,14 +323,14 @@ extern "C" int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_
   }
 
   // ---- layout: the arrays in order, each on a 4-int32 boundary ----
-  const int64_t sizes[15] = {int64_t(njobs) * maxr, njobs, njobs, njobs, int64_t(nreq) * maxs, nreq,
+  const int64_t sizes[14] = {int64_t(njobs) * maxr, njobs, njobs, njobs, int64_t(nreq) * maxs, nreq,
                              int64_t(npieces) * 4, nreq, int64_t(nreq) * maxp,
                              int64_t(small[0].size() + small[1].size() + small[2].size()) * 2,
                              int64_t(tc.size()), int64_t(kn_offsets.size()), int64_t(kn_tasks.size()),
-                             int64_t(segs.size()), kQueueWords};
-  int64_t offs[15];
+                             int64_t(segs.size())};
+  int64_t offs[14];
   int64_t total = 0;
-  for (int a = 0; a < 15; ++a) {
+  for (int a = 0; a < 14; ++a) {
     total += (4 - total % 4) % 4;
     offs[a] = total;
     total += sizes[a];
@@ -358,11 +357,11 @@ extern "C" int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_
   L.small_class_end[2] = L.num_small_tasks;
   L.small_max_keys = small_max_keys;
   L.kstart_stride = 1;
-  int32_t* const off_fields[15] = {&L.off_qids, &L.off_kstart, &L.off_qlen, &L.off_klen, &L.off_slots,
+  int32_t* const off_fields[14] = {&L.off_qids, &L.off_kstart, &L.off_qlen, &L.off_klen, &L.off_slots,
                                    &L.off_counts, &L.off_pieces, &L.off_pcounts, &L.off_cslots,
                                    &L.off_small_tasks, &L.off_tc_tasks, &L.off_kn_offsets, &L.off_kn_tasks,
-                                   &L.off_kn_segs, &L.off_queue};
-  for (int a = 0; a < 15; ++a) *off_fields[a] = int32_t(offs[a]);
+                                   &L.off_kn_segs};
+  for (int a = 0; a < 14; ++a) *off_fields[a] = int32_t(offs[a]);
   *layout = L;
   if (!meta || meta_capacity < total) return TA_ERR_TOO_LARGE;
 
@@ -412,6 +411,5 @@ extern "C" int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_
   std::copy(kn_offsets.begin(), kn_offsets.end(), meta + offs[11]);
   std::copy(kn_tasks.begin(), kn_tasks.end(), meta + offs[12]);
   std::copy(segs.begin(), segs.end(), meta + offs[13]);
-  // queue (offs[14]) stays zero
   return TA_OK;
 }

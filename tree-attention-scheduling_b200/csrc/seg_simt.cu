@@ -35,7 +35,7 @@ struct SimtSmem {
   static constexpr size_t off_stage = 0;
   static constexpr size_t off_mz = off_stage + STAGES * stage_bytes;   // [4 warps][R] max, then sum
   static constexpr size_t off_bar = (off_mz + 2 * kWarps * R * 4 + 15) / 16 * 16;
-  static constexpr size_t bytes = off_bar + 2 * STAGES * 8;
+  static constexpr size_t bytes = off_bar + (2 * STAGES + 1) * 8;        // full, empty, never
   static_assert(size_t(kWarps) * R * D * 4 <= STAGES * stage_bytes, "warp combine reuses the chunk buffers");
 };
 
@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::off_bar);
   uint64_t* empty = full + STAGES;
+  uint64_t* never = empty + STAGES;                    // a barrier nothing arrives on (p.test_stall)
   float* mz = reinterpret_cast<float*>(smem + L::off_mz);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -92,7 +93,9 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
   const uint16_t* vbase = p.v + (int64_t(head) * p.pool_tokens + k0) * D;
   auto stage_k = [&](int s) { return reinterpret_cast<uint16_t*>(smem + L::off_stage + s * L::stage_bytes); };
   auto stage_v = [&](int s) { return stage_k(s) + kChunk * D; };
+  int issued = 0;                                      // thread 0: chunks issued
   auto issue = [&](int c) {
+    ++issued;
     const int keys = min(kChunk, nk - c * kChunk);
     const uint32_t bytes = uint32_t(keys) * D * 2;
     const int st = c % STAGES;
@@ -107,6 +110,7 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kWarps);
     }
+    mbar_init(never, 1);
     fence_barrier_init();
     for (int c = 0; c < min(nchunks, STAGES); ++c) issue(c);
   }
@@ -141,11 +145,17 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
     for (int e = 0; e < DL; ++e) acc[r][e] = 0.f;
 
   bool alive = true;
+  int consumed = 0;                                    // chunks whose copies this warp saw land
   for (int c = 0; c < nchunks; ++c) {
     const int st = c % STAGES;
     const int keys = min(kChunk, nk - c * kChunk);
+    // Test hook: wait on a barrier that nothing completes, so the bounded wait
+    // gives up with TA_ERR_TIMEOUT and the error path below runs.
+    if (p.test_stall && c == 0) alive = __all_sync(0xffffffffu, mbar_wait(never, 0, p.status));
+    if (!alive) break;
     alive = __all_sync(0xffffffffu, mbar_wait(&full[st], (c / STAGES) & 1, p.status));
     if (!alive) break;
+    consumed = c + 1;
     const uint16_t* kc = stage_k(st);
     const uint16_t* vc = stage_v(st);
     const int kw = warp * kKeysPerWarp;                  // this warp's first key in the chunk
@@ -224,8 +234,13 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
     }
   }
 
-  // -- combine the four warps (reusing the chunk buffers: every issued chunk
-  // has been consumed, so no copy is in flight) and publish
+  // -- combine the four warps (reusing the chunk buffers) and publish.  After
+  // a wait gave up, copies may still be in flight: they must land before the
+  // buffers are reused or the CTA exits.  Thread 0 waits (bounded) for every
+  // chunk it issued past the ones its warp saw land.
+  __syncthreads();
+  if (tid == 0)
+    for (int c = consumed; c < issued; ++c) mbar_wait(&full[c % STAGES], (c / STAGES) & 1, p.status);
   __syncthreads();
   float* red = reinterpret_cast<float*>(smem + L::off_stage);
   if (lane < R) {

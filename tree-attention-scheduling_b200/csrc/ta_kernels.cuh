@@ -24,13 +24,13 @@ struct SegParams {
   const int32_t* kn_tasks;     // [n, 4] task headers
   const int32_t* kn_segs;      // [m, 8] segments
   int32_t* status;
-  int32_t* queue;            // [4] work-queue counters of the small-group kernel (zero between calls)
   int64_t pool_tokens;
   int32_t num_jobs, num_pieces, max_requests, kstart_stride, num_requests, num_partials;
   int32_t num_q_heads, num_kv_heads, group;
   int32_t num_kn_tasks, num_kn_segs, kn_ctas;
   int32_t kn_cta_base;         // first kn_offsets entry of the current keys-in-lanes launch
   int32_t kn_after_tc;         // the keys-in-lanes launches follow a query-tile launch of the same call
+  int32_t test_stall;        // test hook: the SIMT kernel's waits give up (TA_ERR_TIMEOUT)
   float scale_log2;          // log2(e) / sqrt(D)
   uint32_t gmul;             // ceil(65536 / group): x / group == (x * gmul) >> 16 for x < 65536 / group
 };
@@ -113,9 +113,6 @@ cudaError_t launch_seg_simt(const SegParams& p, const int32_t class_end[3], int 
                             cudaStream_t stream);
 cudaError_t launch_seg_tc(const SegParams& p, int num_tasks, int dtype, cudaStream_t stream);
 cudaError_t launch_seg_kn(const SegParams& p, const int32_t class_ctas[5], int dtype, cudaStream_t stream);
-// The small-group kernel over the plan's kn_segs; with `merge` it also runs
-// the LSE merge of the step as its last phase.
-cudaError_t launch_seg_stream(const SegParams& p, const MergeParams* merge, int dtype, cudaStream_t stream);
 cudaError_t launch_merge(const MergeParams& p, int head_dim, int dtype, cudaStream_t stream);
 cudaError_t launch_fill_klen(int32_t* klen, const int32_t* idx, int n, int value, int num_jobs, int32_t* status,
                              cudaStream_t stream);

@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libtree_attn_b200.so")
-ABI_VERSION = 6
+ABI_VERSION = 5
 
 DTYPE_BF16 = 1
 DTYPE_F16 = 2
@@ -47,7 +47,7 @@ class PlanLayout(ctypes.Structure):
     _fields_ += [(name, ctypes.c_int32) for name in (
         "small_max_keys", "kstart_stride", "off_qids", "off_kstart", "off_qlen", "off_klen", "off_slots",
         "off_counts", "off_pieces", "off_pcounts", "off_cslots", "off_small_tasks", "off_tc_tasks",
-        "off_kn_offsets", "off_kn_tasks", "off_kn_segs", "off_queue")]
+        "off_kn_offsets", "off_kn_tasks", "off_kn_segs")]
 
 
 class CostModelC(ctypes.Structure):

@@ -366,16 +366,13 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
     kn_segs = np.array(segs, dtype=np.int32).reshape(-1, 12)
     return dict(qids=qids, kids=kids, qlen=qlen, klen=klen, slots=slots, counts=counts,
                 pieces=pieces, pcounts=pcounts, cslots=cslots, small_tasks=small_tasks, tc_tasks=tc_tasks,
-                kn_offsets=kn_offsets, kn_tasks=kn_tasks, kn_segs=kn_segs,
-                queue=np.zeros(QUEUE_WORDS, dtype=np.int32), small_class_end=class_end,
+                kn_offsets=kn_offsets, kn_tasks=kn_tasks, kn_segs=kn_segs, small_class_end=class_end,
                 small_max_keys=small_max_keys, kn_ctas=kn_ctas, kn_class_ctas=kn_class_ctas, contiguous_k=contiguous_k,
                 num_partials=slot)
 
 
 _ORDER = ("qids", "kids", "qlen", "klen", "slots", "counts", "pieces", "pcounts", "cslots", "small_tasks",
-          "tc_tasks", "kn_offsets", "kn_tasks", "kn_segs", "queue")
-# Work-queue counters of the small-group kernel (zero between calls).
-QUEUE_WORDS = 4
+          "tc_tasks", "kn_offsets", "kn_tasks", "kn_segs")
 
 
 def _sm_count(device):
@@ -391,8 +388,7 @@ _SHAPES = {
     "pieces": lambda L: (L.num_pieces, 4), "pcounts": lambda L: (L.num_requests,),
     "cslots": lambda L: (L.num_requests, L.max_pslots), "small_tasks": lambda L: (L.num_small_tasks, 2),
     "tc_tasks": lambda L: (L.num_tc_tasks, 4), "kn_offsets": lambda L: (L.kn_ctas + 1,),
-    "kn_tasks": lambda L: (L.num_kn_tasks, 4), "kn_segs": lambda L: (L.num_kn_segs, 12),
-    "queue": lambda L: (QUEUE_WORDS,)}
+    "kn_tasks": lambda L: (L.num_kn_tasks, 4), "kn_segs": lambda L: (L.num_kn_segs, 12)}
 _OFFSET_FIELD = {name: "off_" + ("kstart" if name == "kids" else name) for name in _ORDER}
 
 
