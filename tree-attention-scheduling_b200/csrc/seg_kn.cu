@@ -345,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
                  "r"(C::kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -951,6 +952,8 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
     if (pend_k >= 0) epilogue(pend_k, pend_g, (qi - 1) & 1);
   }
 
+  // Every warp reconverges (roles ran on one lane) before the CTA-wide barrier.
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {

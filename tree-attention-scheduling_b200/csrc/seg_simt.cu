@@ -237,10 +237,13 @@ __global__ void __launch_bounds__(kThreads) seg_simt_kernel(SegParams p, int tas
   // -- combine the four warps (reusing the chunk buffers) and publish.  After
   // a wait gave up, copies may still be in flight: they must land before the
   // buffers are reused or the CTA exits.  Thread 0 waits (bounded) for every
-  // chunk it issued past the ones its warp saw land.
+  // chunk it issued past the ones its warp saw land.  (Each warp reconverges
+  // before a CTA-wide barrier.)
+  __syncwarp();
   __syncthreads();
   if (tid == 0)
     for (int c = consumed; c < issued; ++c) mbar_wait(&full[c % STAGES], (c / STAGES) & 1, p.status);
+  __syncwarp();
   __syncthreads();
   float* red = reinterpret_cast<float*>(smem + L::off_stage);
   if (lane < R) {

@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -546,6 +547,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // Every warp reconverges (roles ran on one lane) before the CTA-wide barrier.
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
