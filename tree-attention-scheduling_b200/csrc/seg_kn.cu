@@ -317,6 +317,16 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
   }
   const int count = end - begin;
   auto slot_of = [&](int k) { return tasks + (k % kTQ) * kTaskWords; };   // k: index within this CTA's list
+  // The scheduler's first loads (two task headers, the first task's segment
+  // records) overlap the set-up below.
+  int4 first_hdr = make_int4(0, 0, 0, 0), second_hdr = first_hdr, first_rec = first_hdr;
+  if (warp == kSchedWarp && count > 0) {
+    first_hdr = load_header(p, begin);
+    if (count > 1) second_hdr = load_header(p, begin + 1);
+    if (first_hdr.y >= 1 && first_hdr.y <= kSegMax && first_hdr.x >= 0 &&
+        int64_t(first_hdr.x) + first_hdr.y <= p.num_kn_segs && lane < 3 * first_hdr.y)
+      first_rec = reinterpret_cast<const int4*>(p.kn_segs)[3 * int64_t(first_hdr.x) + lane];
+  }
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -381,10 +391,9 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
       return __shfl_sync(0xffffffffu, ok, 0) != 0;
     };
     auto header_ok = [&](int4 h) { return h.y >= 1 && h.y <= kSegMax && h.x >= 0 && int64_t(h.x) + h.y <= p.num_kn_segs; };
-    int4 hdr = count > 0 ? load_header(p, begin) : make_int4(0, 0, 0, 0);
-    if (count > 0 && header_ok(hdr) && lane < 3 * hdr.y)
-      stage[lane] = reinterpret_cast<const int4*>(p.kn_segs)[3 * int64_t(hdr.x) + lane];
-    int4 hdr_next = count > 1 ? load_header(p, begin + 1) : make_int4(0, 0, 0, 0);
+    int4 hdr = first_hdr;
+    if (count > 0 && header_ok(hdr) && lane < 3 * hdr.y) stage[lane] = first_rec;
+    int4 hdr_next = second_hdr;
     __syncwarp();
     for (int k = 0; k < count && alive; ++k) {
       int* w = slot_of(k);
@@ -436,6 +445,14 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
                          s >= 0 ? p.q + s + c * 8 : p.q, s >= 0 ? 16u : 0u);
       }
       cp_async_commit();
+      if (qi == 0) {                     // the first Q^T: nothing else is ready, publish it at once
+        cp_async_wait_group<0>();
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full[qb]);
+        ++qi;
+        continue;
+      }
       if (pending_qb >= 0) {             // the previous task's copies: the older group
         cp_async_wait_group<1>();
         fence_async_smem();
