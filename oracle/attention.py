@@ -28,9 +28,11 @@ def _scores(qr, kr, dim):
 def request_attention(q, k, v, paths, return_lse=False):
     """Per-request FP32 attention (reference.py:4-13).
 
-    Returns the output in ``q.dtype``; with ``return_lse`` also the float32
-    output and the natural-log LSE ``[NREQ, HQ]``.
+    ``paths``: the requests' token paths, or the ``KVTree`` itself (the
+    reference's argument).  Returns the output in ``q.dtype``; with
+    ``return_lse`` also the float32 output and the natural-log LSE ``[NREQ, HQ]``.
     """
+    paths = getattr(paths, "paths", paths)
     groups = q.shape[1] // k.shape[1]
     dim = q.shape[-1]
     outs, lses = [], []
@@ -78,7 +80,11 @@ def merge_partials(num_requests, jobs, partials):
 
 
 def segmented_attention(q, k, v, jobs, return_lse=False):
-    """Plan-driven FP32 attention with the global LSE merge (reference.py:16-33)."""
+    """Plan-driven FP32 attention with the global LSE merge (reference.py:16-33).
+
+    ``jobs``: the plan's jobs, or the ``Plan`` itself (the reference's argument).
+    """
+    jobs = getattr(jobs, "jobs", jobs)
     out, lse = merge_partials(q.shape[0], jobs, job_partials(q, k, v, jobs))
     if return_lse:
         return out.to(q.dtype), out, lse

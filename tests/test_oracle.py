@@ -69,3 +69,15 @@ def test_oracle_detects_planted_error():
     good = oracle.request_attention(q, k, v, tree.paths)
     bad = oracle.segmented_attention(q, k, v, broken)
     assert not torch.allclose(good, bad, atol=1e-3)
+
+
+def test_oracle_takes_the_reference_arguments():
+    """The reference's scripts call reference.request_attention(q, k, v, tree) and
+    segmented_attention(q, k, v, plan): the oracle accepts those objects too."""
+    case = CASES[0]
+    name, qh, kh, d, _ = case.split("|")
+    tree = build_tree(_Lib, SPECS[name])
+    q, k, v = (load_bf16(f"{case}|{t}") for t in "qkv")
+    plan = schedule(tree, int(qh), int(kh), int(d), "cube", CostModel(kv_split=48) if int(d) == 32 else CostModel())
+    assert torch.equal(oracle.request_attention(q, k, v, tree), oracle.request_attention(q, k, v, tree.paths))
+    assert torch.equal(oracle.segmented_attention(q, k, v, plan), oracle.segmented_attention(q, k, v, plan.jobs))

@@ -17,6 +17,17 @@ branching factor with the evaluation grid the fitted model is evaluated on.
 calibration trees 48.4 -> 47.6 us); no other single change among ``SEARCH``
 gained more than 1%.  On the evaluation grid and the headline shape the two
 settings measure the same within noise.
+
+How the partial count enters the model: the scheduler cuts every job into
+physical jobs of at most ``kv_split`` tokens, and each physical job pays its
+partial-output term and ``merge_us`` per request, so the key-range cutting the
+kernels need (8 root pieces of 1024 tokens at the headline) is costed.  The
+execution-piece split in ``kernels.split_pieces`` cuts further only when a
+plan's query-tile CTAs would leave SMs idle, i.e. when the step is short of
+work rather than of bandwidth; it adds no piece at the headline (16 root jobs
+x 8 KV heads = 128 CTAs).  ``key_tile`` (the small-group key tile) is searched
+at 128, the keys-in-lanes kernel's tile, and at 256; 128 did not gain the fit's
+1% threshold, so 256 stayed.
 """
 import math
 from dataclasses import asdict
