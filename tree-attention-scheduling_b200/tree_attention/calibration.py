@@ -16,7 +16,11 @@ branching factor with the evaluation grid the fitted model is evaluated on.
 ``max_query_rows`` from 512 to 256 (geometric-mean step time of the 24
 calibration trees 48.4 -> 47.6 us); no other single change among ``SEARCH``
 gained more than 1%.  On the evaluation grid and the headline shape the two
-settings measure the same within noise.
+settings measure the same within noise.  Re-run on the current kernels
+(``bench.py --config calibrate``: 25 candidates, 35 s on one B200) the
+constants stay a coordinate-wise optimum: geometric mean 47.8 us; the best
+single changes were cube_rows 64 (47.9 us) and 32 (47.9 us), key_tile 128
+48.2 us.
 
 How the partial count enters the model: the scheduler cuts every job into
 physical jobs of at most ``kv_split`` tokens, and each physical job pays its
