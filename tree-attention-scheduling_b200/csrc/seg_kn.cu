@@ -416,8 +416,9 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
       if (qi >= QB && !wait_or_flush(&q_empty[qb], ((qi / QB) - 1) & 1)) { alive = false; break; }
       // Each lane finds the Q row behind tile rows lane and lane + 32, then the
       // warp copies rows x 16 chunks of 16 bytes, swizzled K-major, with
-      // asynchronous copies (zero-filled where a row is out of range).  This
-      // task's Q^T is published once the next task's copies are issued (or
+      // asynchronous copies (zero-filled where a row is out of range).  The
+      // first task's Q^T is published as soon as it lands (nothing else is
+      // ready yet); a later task's once the next task's copies are issued (or
       // before the warp blocks), so the copy latency of consecutive tasks
       // overlaps.
       const int rows = t.rows;
