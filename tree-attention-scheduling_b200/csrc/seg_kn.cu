@@ -820,7 +820,8 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
 #pragma unroll
               for (int q = 0; q < CW; ++q) {
                 const int r = c * CW + q;
-                need |= ((live_rows >> r) & 1ull) && __uint_as_float(raw[q]) * scale > m[r] + kRescaleThreshold;
+                if (j > 0)              // (a task's first tile always sets the maxima)
+                  need |= ((live_rows >> r) & 1ull) && __uint_as_float(raw[q]) * scale > m[r] + kRescaleThreshold;
                 if (c == 0) keep[q] = raw[q];
               }
             }
@@ -881,13 +882,26 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
 #pragma unroll
           for (int c = 0; c < NC; ++c) {
             if (c * CW < rows) {
+              // the four warps' maxima of four rows per vector load
+              float mt[CW];
+#pragma unroll
+              for (int q = 0; q < CW; q += 4) {
+                const float4 w0 = *reinterpret_cast<const float4*>(rt + c * CW + q);
+                const float4 w1 = *reinterpret_cast<const float4*>(rt + R + c * CW + q);
+                const float4 w2 = *reinterpret_cast<const float4*>(rt + 2 * R + c * CW + q);
+                const float4 w3 = *reinterpret_cast<const float4*>(rt + 3 * R + c * CW + q);
+                mt[q] = fmaxf(fmaxf(w0.x, w1.x), fmaxf(w2.x, w3.x));
+                mt[q + 1] = fmaxf(fmaxf(w0.y, w1.y), fmaxf(w2.y, w3.y));
+                mt[q + 2] = fmaxf(fmaxf(w0.z, w1.z), fmaxf(w2.z, w3.z));
+                mt[q + 3] = fmaxf(fmaxf(w0.w, w1.w), fmaxf(w2.w, w3.w));
+              }
               float alpha[CW];
 #pragma unroll
-              for (int q = 0; q < CW; ++q) {       // no stores in this loop: the loads batch
+              for (int q = 0; q < CW; ++q) {
                 const int r = c * CW + q;
-                const float mt = fmaxf(fmaxf(rt[r], rt[R + r]), fmaxf(rt[2 * R + r], rt[3 * R + r]));
-                const float mn = fmaxf(m[r], mt);
-                alpha[q] = mn != -INFINITY ? fast_exp2(m[r] - mn) : 1.f;   // m = -inf gives 0
+                const float mn = fmaxf(m[r], mt[q]);
+                // a task's first tile has no sum or output to rescale yet
+                alpha[q] = (j > 0 && mn != -INFINITY) ? fast_exp2(m[r] - mn) : 1.f;   // m = -inf gives 0
                 l[r] *= alpha[q];
                 m[r] = mn;                  // rows past `rows` have no live key and stay at -inf
               }
