@@ -238,13 +238,11 @@ __device__ __forceinline__ uint32_t swz(uint32_t half, int r, int c) {
          uint32_t(c & 7) * 2u;
 }
 
-// Float max over the warp as an order-preserving unsigned key (redux.sync).
+// Float max over the warp (sm_100a redux.sync on f32; -inf for a row with no live key).
 __device__ __forceinline__ float warp_max_redux(float x) {
-  const uint32_t b = __float_as_uint(x);
-  const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  uint32_t r;
-  asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(k));
-  return __uint_as_float((r & 0x80000000u) ? (r & 0x7fffffffu) : ~r);
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x));
+  return r;
 }
 
 // W consecutive 32-bit TMEM columns of this thread's lane (W = 4, 8 or 16).
