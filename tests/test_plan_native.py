@@ -82,6 +82,23 @@ def test_native_builder_matches_on_headline_plans():
         for sms in (148, 132, 16):
             assert_native_matches(jobs, 128, 4, True, 8, sms)
         assert_native_matches(jobs, 128, 4, True, 4, 148)   # a two-GPU KV-head shard
+        for heads in (2, 1):                                   # four- and eight-GPU shards
+            assert_native_matches(jobs, 128, 4, True, heads, 148)
+
+
+def test_query_tile_cut_level_follows_the_step_model():
+    """The headline cube plan on one GPU keeps the widest cut (16 jobs x 8 heads = 128 query-tile CTAs,
+    keys-in-lanes after them on 296 CTAs); a four-GPU shard (2 KV heads) stops one level earlier (96 CTAs
+    of 3 tiles) and places the 128 keys-in-lanes tasks on the 104 CTAs the 52 free SMs hold."""
+    tree = build_tree(_Lib, next(s for s in TREE_SPECS if s["name"] == "headline"))
+    jobs = sorted_jobs(schedule(tree, 32, 8, 128, "cube", CostModel.b200()), 4)
+    for heads, tc_ctas, kn_ctas in ((8, 128, 296), (4, 128, 256), (2, 96, 104), (1, 64, 64)):
+        meta = kernels.build_metadata(jobs, 128, 4, True, heads=heads, sms=148)
+        assert (len(meta["tc_tasks"]) * heads, int(meta["kn_ctas"])) == (tc_ctas, kn_ctas), heads
+    levels = [(32, 8), (64, 4), (96, 3), (128, 2)]
+    assert kernels.choose_tc_level(levels, [0, 128, 0, 0, 0], 148) == (96, 96)
+    assert kernels.choose_tc_level([(128, 8)], [0, 512, 0, 0, 0], 148) == (None, None)
+    assert kernels.choose_tc_level([], [0, 512, 0, 0, 0], 148) == (None, None)
 
 
 def test_native_builder_matches_with_decode_tails():

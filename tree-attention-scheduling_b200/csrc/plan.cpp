@@ -59,9 +59,12 @@ struct Item {
 // Execution pieces: kn jobs cut so no piece holds more than about half a CTA's
 // share of all key tiles; query-tile jobs cut a whole level of the longest
 // pieces at a time while their CTAs fit one wave.
+// tc_max_ctas (<= 0: none) caps the query-tile CTAs below sms; levels, if
+// given, receives (query-tile CTAs, longest piece in tiles) of every level.
 void split_pieces(int njobs, const std::vector<int>& rows, const std::vector<int>& route,
                   const int32_t* keys, const std::vector<char>& splittable, int heads, int sms,
-                  std::vector<PieceRec>& pieces) {
+                  std::vector<PieceRec>& pieces, int64_t tc_max_ctas = 0,
+                  std::vector<std::pair<int64_t, int64_t>>* levels = nullptr) {
   std::vector<int> count(njobs, 1);
   int64_t total = 0;
   bool any_kn = false;
@@ -85,12 +88,14 @@ void split_pieces(int njobs, const std::vector<int>& rows, const std::vector<int
       ctas += pairs[i];
       any_tc = true;
     }
+  const int64_t limit = tc_max_ctas > 0 ? std::min<int64_t>(sms, tc_max_ctas) : int64_t(sms);
   while (any_tc) {
     // one level: every query-tile job whose pieces are the longest takes one
     // more piece, if all of them can and the CTAs still fit one wave
     int64_t longest = 0;
     for (int i = 0; i < njobs; ++i)
       if (route[i] == kTc) longest = std::max(longest, cdiv(tiles_of(keys[i]), count[i]));
+    if (levels) levels->push_back({ctas, longest});
     bool ok = true;
     int64_t extra = 0;
     for (int i = 0; i < njobs && ok; ++i) {
@@ -98,7 +103,7 @@ void split_pieces(int njobs, const std::vector<int>& rows, const std::vector<int
       ok = splittable[i] && double(tiles_of(keys[i])) / double(count[i] + 1) >= 2.0;
       extra += pairs[i];
     }
-    if (!ok || ctas + extra > sms) break;
+    if (!ok || ctas + extra > limit) break;
     for (int i = 0; i < njobs; ++i)
       if (route[i] == kTc && cdiv(tiles_of(keys[i]), count[i]) == longest) count[i] += 1;
     ctas += extra;
@@ -172,6 +177,80 @@ std::vector<std::vector<int>> pack_segments(const std::vector<Item>& items) {
   return tasks;
 }
 
+// Step-time model that picks how far query-tile jobs are cut (tenths of a
+// microsecond, from steady-state timelines of the two kernels on one B200):
+// a query-tile CTA costs kTcFixed plus kTcPerTile per K/V tile of its piece;
+// a keys-in-lanes CTA costs kKnFixed plus kKnPerTask per task it runs.
+constexpr int64_t kTcFixed = 70, kTcPerTile = 22, kKnFixed = 25, kKnPerTask = 35;
+
+// Keys-in-lanes tasks per row class of a piece list (the packing below).
+void kn_class_counts(const std::vector<PieceRec>& plist, const std::vector<int>& route, const std::vector<int>& rows,
+                     int groups, int heads, int64_t counts[5]) {
+  const int chunk = std::max(groups, kKnTaskRows / groups * groups);
+  std::vector<Item> items;
+  for (const PieceRec& pc : plist) {
+    if (route[pc.job] != kKn) continue;
+    for (int h = 0; h < heads; ++h)
+      for (int r0 = 0; r0 < rows[pc.job]; r0 += chunk)
+        items.push_back({{h, std::min(chunk, rows[pc.job] - r0), 0, 0, pc.take, 0, -1, 0}});
+  }
+  for (int c = 0; c < 5; ++c) counts[c] = 0;
+  for (const auto& task : pack_segments(items)) {
+    int r = 0;
+    for (int idx : task) r += items[idx].rows();
+    const int c = kn_class(r);
+    if (c >= 0) ++counts[c];
+  }
+}
+
+// Cut level of the query-tile jobs and keys-in-lanes placement with the
+// lowest modelled step time: after the query tiles (each class over
+// min(kKnDualCtas * sms, tasks) CTAs, the default) or, with one row class,
+// beside them on the SMs they leave free.  cap: query-tile CTA cap (0: none);
+// beside: query-tile CTAs the keys-in-lanes CTAs are sized against (-1: default
+// placement).  Ties keep more query-tile CTAs, then the default placement.
+void choose_tc_level(const std::vector<std::pair<int64_t, int64_t>>& levels, const int64_t counts[5], int sms,
+                     int64_t& cap, int64_t& beside) {
+  cap = 0;
+  beside = -1;
+  if (levels.empty()) return;
+  int used = 0, last = -1;
+  for (int c = 0; c < 5; ++c)
+    if (counts[c] > 0) {
+      ++used;
+      last = c;
+    }
+  auto per_sm = [](int c) { return kKnClassRows[c] <= kKnDualRows ? kKnDualCtas : 1; };
+  int64_t best_t = 0;
+  int best_index = -1, best_mode = 0;
+  auto consider = [&](int64_t t, int index, int mode) {
+    // key (t, -index, mode), lexicographically smallest
+    if (best_index < 0 || t < best_t || (t == best_t && (index > best_index || (index == best_index && mode < best_mode)))) {
+      best_t = t;
+      best_index = index;
+      best_mode = mode;
+    }
+  };
+  for (int index = 0; index < int(levels.size()); ++index) {
+    const int64_t ctas = levels[index].first;
+    const int64_t t_tc = kTcFixed + kTcPerTile * levels[index].second;
+    if (used == 0) {
+      consider(t_tc, index, 0);
+      continue;
+    }
+    int64_t rounds = 0;
+    for (int c = 0; c < 5; ++c)
+      if (counts[c] > 0) rounds = std::max(rounds, cdiv(counts[c], std::min<int64_t>(int64_t(per_sm(c)) * sms, counts[c])));
+    consider(t_tc + kKnFixed + kKnPerTask * rounds, index, 0);
+    if (used == 1 && sms > ctas) {
+      const int64_t side = std::min<int64_t>(int64_t(per_sm(last)) * (sms - ctas), counts[last]);
+      consider(std::max(t_tc, kKnFixed + kKnPerTask * cdiv(counts[last], side)), index, 1);
+    }
+  }
+  cap = best_index == int(levels.size()) - 1 ? 0 : levels[best_index].first;
+  beside = best_mode ? levels[best_index].first : -1;
+}
+
 // Longest-processing-time assignment of tasks to `bins` persistent CTAs: tasks
 // by decreasing cost (ties in input order), each to the least-loaded CTA (ties:
 // the lowest CTA index).  offsets [bins + 1]; CTA b runs order[offsets[b]..).
@@ -235,7 +314,16 @@ extern "C" int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_
     splittable[i] = no_split_from < 0 || job_k0[i] < no_split_from;
   }
   std::vector<PieceRec> plist;
-  split_pieces(njobs, rows, route, job_keys, splittable, num_kv_heads, sms, plist);
+  std::vector<std::pair<int64_t, int64_t>> levels;
+  split_pieces(njobs, rows, route, job_keys, splittable, num_kv_heads, sms, plist, 0, &levels);
+  int64_t kn_counts[5];
+  kn_class_counts(plist, route, rows, groups, num_kv_heads, kn_counts);
+  int64_t tc_cap = 0, kn_beside = -1;
+  choose_tc_level(levels, kn_counts, sms, tc_cap, kn_beside);
+  if (tc_cap > 0) {
+    plist.clear();
+    split_pieces(njobs, rows, route, job_keys, splittable, num_kv_heads, sms, plist, tc_cap);
+  }
   const int npieces = int(plist.size());
   std::vector<int32_t> piece_slot(npieces);
   std::vector<int> pcounts(nreq, 0);
@@ -307,7 +395,9 @@ extern "C" int ta_plan_build(const int32_t* job_req_offsets, const int32_t* job_
     for (int c = 0; c < 5; ++c) {
       const auto& entries = by_class[c];
       if (entries.empty()) continue;
-      const int ctas = int(std::min<int64_t>(int64_t(sms) * (kKnClassRows[c] <= kKnDualRows ? kKnDualCtas : 1),
+      // beside the query tiles (kn_beside >= 0): on the SMs they leave free
+      const int64_t free_sms = kn_beside >= 0 ? int64_t(sms) - kn_beside : int64_t(sms);
+      const int ctas = int(std::min<int64_t>(free_sms * (kKnClassRows[c] <= kKnDualRows ? kKnDualCtas : 1),
                                              int64_t(entries.size())));
       costs.clear();
       for (const auto& e : entries) costs.push_back(e.second);

@@ -107,7 +107,7 @@ def _tiles(keys):
     return max(1, -(-keys // KEY_TILE))
 
 
-def split_pieces(jobs, groups, heads, use_tc, sms, no_split_from=None):
+def split_pieces(jobs, groups, heads, use_tc, sms, no_split_from=None, tc_max_ctas=None, levels=None):
     """Cut jobs into execution pieces ``(job, key_offset, keys)`` so the kernels fill the GPU.
 
     A piece is a contiguous key range of one job with its own partial slots;
@@ -118,6 +118,9 @@ def split_pieces(jobs, groups, heads, use_tc, sms, no_split_from=None):
     their CTAs still fit one wave on ``sms`` SMs, a whole level of the longest
     pieces at a time.  Jobs whose first position is
     at or past ``no_split_from`` (the growing decode tails) stay whole.
+    ``tc_max_ctas`` caps the query-tile CTAs below ``sms``; ``levels``, if a
+    list, receives ``(query-tile CTAs, longest piece in key tiles)`` of every
+    level the cutting passes through.
     """
     n = len(jobs)
     rows = [len(j.requests) * groups for j in jobs]
@@ -143,13 +146,16 @@ def split_pieces(jobs, groups, heads, use_tc, sms, no_split_from=None):
         # beside the query-tile kernel.
         pairs = {i: -(-rows[i] // TC_ROWS) * heads for i in tc}
         ctas = sum(pairs.values())
+        limit = sms if tc_max_ctas is None else min(sms, tc_max_ctas)
         while True:
             longest = max(-(-_tiles(keys[i]) // count[i]) for i in tc)
+            if levels is not None:
+                levels.append((ctas, longest))
             level = [i for i in tc if -(-_tiles(keys[i]) // count[i]) == longest]
             if not all(splittable[i] and _tiles(keys[i]) / (count[i] + 1) >= 2 for i in level):
                 break
             extra = sum(pairs[i] for i in level)
-            if ctas + extra > sms:
+            if ctas + extra > limit:
                 break
             for i in level:
                 count[i] += 1
@@ -239,6 +245,68 @@ def pack_segments(items):
     return tasks
 
 
+# Step-time model that picks how far query-tile jobs are cut (tenths of a
+# microsecond, from steady-state timelines of the two kernels on one B200):
+# a query-tile CTA costs TC_FIXED plus TC_PER_TILE per K/V tile of its piece;
+# a keys-in-lanes CTA costs KN_FIXED plus KN_PER_TASK per task it runs.
+TC_FIXED, TC_PER_TILE, KN_FIXED, KN_PER_TASK = 70, 22, 25, 35
+
+
+def kn_class_counts(jobs, piece_list, route, rows, groups, heads):
+    """Keys-in-lanes tasks per row class of a piece list (the packing of ``build_metadata``)."""
+    chunk = max(groups, KN_TASK_ROWS // groups * groups)
+    items = []
+    for i, offset, take in piece_list:
+        if route[i] == "kn":
+            for h in range(heads):
+                for r0 in range(0, rows[i], chunk):
+                    items.append((h, min(chunk, rows[i] - r0), 0, 0, take, 0, -1, 0))
+    counts = [0] * len(KN_CLASS_ROWS)
+    for task in pack_segments(items):
+        counts[kn_class(sum(item[1] for item in task))] += 1
+    return counts
+
+
+def choose_tc_level(levels, class_counts, sms):
+    """Cut level of the query-tile jobs and keys-in-lanes placement with the lowest modelled step time.
+
+    ``levels``: ``(query-tile CTAs, longest piece in tiles)`` per cut level
+    (``split_pieces``), coarsest first.  Two placements of the keys-in-lanes
+    tasks are weighed: after the query tiles, each class over
+    ``min(KN_DUAL_CTAS * sms, tasks)`` CTAs (the default), or - with one row
+    class - beside them, on ``KN_DUAL_CTAS`` CTAs per SM the query tiles leave
+    free, all placed when the launch is (CTAs placed later wait for the
+    query-tile grid to finish).  Returns ``(cap, beside)``: the query-tile CTA
+    cap for ``split_pieces`` (None: no cap) and, for the beside placement, the
+    query-tile CTA count the keys-in-lanes CTAs are sized against (else None).
+    Ties keep more query-tile CTAs, then the default placement.
+    """
+    if not levels:
+        return None, None
+    used = [c for c in range(len(KN_CLASS_ROWS)) if class_counts[c]]
+    dual = {c: KN_DUAL_CTAS if KN_CLASS_ROWS[c] <= KN_DUAL_ROWS else 1 for c in used}
+    best = None
+    for index, (ctas, longest) in enumerate(levels):
+        t_tc = TC_FIXED + TC_PER_TILE * longest
+        options = []
+        if not used:
+            options.append((t_tc, 0))
+        else:
+            rounds = max(-(-class_counts[c] // min(dual[c] * sms, class_counts[c])) for c in used)
+            options.append((t_tc + KN_FIXED + KN_PER_TASK * rounds, 0))
+            if len(used) == 1 and sms > ctas:
+                c = used[0]
+                side = min(dual[c] * (sms - ctas), class_counts[c])
+                options.append((max(t_tc, KN_FIXED + KN_PER_TASK * -(-class_counts[c] // side)), 1))
+        for t, mode in options:
+            key = (t, -index, mode)
+            if best is None or key < best[0]:
+                best = (key, index, mode)
+    _, index, mode = best
+    cap = None if index == len(levels) - 1 else levels[index][0]
+    return cap, (levels[index][0] if mode else None)
+
+
 def assign_lpt(costs, bins):
     """Longest-processing-time assignment of tasks to ``bins`` persistent CTAs.
 
@@ -293,7 +361,11 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
         slots[r, :len(per_request[r])] = per_request[r]
     counts = np.fromiter((len(s) for s in per_request), dtype=np.int32, count=num_requests)
 
-    piece_list, route, rows = split_pieces(jobs, groups, heads, use_tc, sms, no_split_from)
+    levels = []
+    piece_list, route, rows = split_pieces(jobs, groups, heads, use_tc, sms, no_split_from, levels=levels)
+    tc_cap, kn_beside = choose_tc_level(levels, kn_class_counts(jobs, piece_list, route, rows, groups, heads), sms)
+    if tc_cap is not None:
+        piece_list, route, rows = split_pieces(jobs, groups, heads, use_tc, sms, no_split_from, tc_max_ctas=tc_cap)
     npieces = len(piece_list)
     pieces = np.zeros((npieces, 4), dtype=np.int32)
     per_request_p = [[] for _ in range(num_requests)]
@@ -354,7 +426,9 @@ def build_metadata(jobs, num_requests, groups, use_tc, heads=1, sms=148, no_spli
     for c, entries in enumerate(by_class):
         if not entries:
             continue
-        ctas = min(sms * (KN_DUAL_CTAS if KN_CLASS_ROWS[c] <= KN_DUAL_ROWS else 1), len(entries))
+        per_sm = KN_DUAL_CTAS if KN_CLASS_ROWS[c] <= KN_DUAL_ROWS else 1
+        # beside the query tiles: on the SMs they leave free
+        ctas = min(per_sm * (sms if kn_beside is None else sms - kn_beside), len(entries))
         offs, order = assign_lpt([cost for _, cost in entries], ctas)
         base = len(ordered)
         offsets.extend(int(o) + base for o in offs[1:])
