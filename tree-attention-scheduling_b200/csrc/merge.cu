@@ -16,7 +16,8 @@ namespace {
 constexpr int kMergeWarps = 4;
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(MergeParams p) {
+// (at most 72 registers: seven CTAs per SM hold every (request, head) warp of a 128 x 32 step at once)
+__global__ void __launch_bounds__(kMergeWarps * 32, 7) merge_kernel(MergeParams p) {
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
   const bool active = item < p.num_requests * p.num_q_heads;

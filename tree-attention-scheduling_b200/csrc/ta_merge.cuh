@@ -10,12 +10,13 @@ namespace ta {
 // Merge of one (request, query head) by one warp: lane k loads the LSE of
 // partial k so the maximum and the weights come from warp reductions, then
 // the partial rows are read with independent loads (lanes split head_dim),
-// eight rows in flight.  `count` and `pre_slot` (this lane's first slot, or
+// nine rows in flight.  `count` and `pre_slot` (this lane's first slot, or
 // -1) were loaded by the caller.
 template <typename T, int D>
 __device__ __forceinline__ void merge_one(const MergeParams& p, int request, int head, int count, int pre_slot,
                                           int lane) {
   constexpr int DL = D / 32;
+  constexpr int kBatch = 9;   // partial rows in flight: one round for up to 9 partials (8 root pieces + 1 leaf)
   const int G = p.group, kv_head = head / G, g = head % G;
   const int32_t* slots = p.cslots + int64_t(request) * p.max_slots;
   if (count < 0 || count > p.max_slots) {
@@ -52,13 +53,13 @@ __device__ __forceinline__ void merge_one(const MergeParams& p, int request, int
     m = m_new;
     const float w = fast_exp2((l - m) * kLog2e);        // -inf lse gives 0
     z += warp_sum(w);
-    // every row of the group in flight at once (eight at a time)
+    // the group's rows in flight kBatch at a time
     const int n = min(32, count - k0);
-    for (int j = 0; j < n; j += 8) {
-      float wj[8];
-      float x[8][DL];
+    for (int j = 0; j < n; j += kBatch) {
+      float wj[kBatch];
+      float x[kBatch][DL];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < kBatch; ++u) {
         const int src = min(j + u, n - 1);
         wj[u] = __shfl_sync(0xffffffffu, w, src);
         const int64_t rj = __shfl_sync(0xffffffffu, row, src);
@@ -80,7 +81,7 @@ __device__ __forceinline__ void merge_one(const MergeParams& p, int request, int
         }
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < kBatch; ++u)
 #pragma unroll
         for (int e = 0; e < DL; ++e) acc[e] = fmaf(wj[u], x[u][e], acc[e]);
     }
