@@ -169,10 +169,10 @@ int ta_attention(const ta_plan_layout* plan, const int32_t* meta, const void* q,
 
 /*
  * ta_attention for callers that cannot allocate device memory: no counterpart
- * in the reference, which always allocates its scratch in prepare().  A host
- * that captures its decode step into a CUDA graph in global capture mode, a
- * process whose device memory is owned by another allocator, or a binding
- * without access to a CUDA allocator passes only its inputs and outputs; the
+ * in the reference, which always allocates its scratch in prepare().  A
+ * process whose device memory is owned by another allocator, a binding without
+ * access to a CUDA allocator, or a serving loop that must not allocate on its
+ * decode path passes only its inputs and outputs; the
  * partial outputs and LSEs live in one file-scope device array of
  * TA_NOALLOC_SCRATCH_BYTES per GPU (held by every GPU that loads the library,
  * until exit).  Problems needing more than that -- num_kv_heads * num_partials

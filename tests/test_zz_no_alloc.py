@@ -1,8 +1,8 @@
 """ta_attention_noalloc: the decode-step attention for callers that cannot allocate.
 
-Some hosts cannot call cudaMalloc where they run attention (a decode step
-recorded into a CUDA graph under global capture, a process whose device memory
-belongs to another allocator, a binding with no CUDA allocator).  This entry
+Some hosts cannot call cudaMalloc where they run attention (a process whose
+device memory belongs to another allocator, a binding with no CUDA allocator, a
+serving loop that must not allocate on its decode path).  This entry
 point takes only inputs and outputs and keeps its scratch in a fixed device
 array.  The test calls it through the C ABI twice in a row and checks both
 results against the allocating entry point ta_attention on the same inputs.

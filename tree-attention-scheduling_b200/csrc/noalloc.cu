@@ -2,11 +2,10 @@
 // allocate device memory.
 //
 // Some hosts of this library are not in a position to call cudaMalloc when
-// they run attention: a serving loop that records its whole decode step into
-// a CUDA graph under global capture mode (where allocation calls are illegal),
-// a process whose device memory was handed out up front to another allocator
-// that owns it all, or a foreign-language binding with no handle on a CUDA
-// allocator.  They still own their inputs (queries, pools, plan metadata) and
+// they run attention: a process whose device memory was handed out up front
+// to another allocator that owns it all, a foreign-language binding with no
+// handle on a CUDA allocator, or a latency-bound serving loop that must not
+// allocate (or free) on its decode path.  They still own their inputs (queries, pools, plan metadata) and
 // the output, but not the partial-output / LSE scratch that ta_attention takes
 // as arguments.  This entry point supplies that scratch from one file-scope
 // device array of fixed size instead.
