@@ -289,11 +289,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    // One thread and as few instructions as possible: this warp shares its SM
-    // sub-partition with two busy softmax warps.  Descriptors are precomputed;
-    // per MMA only the 14-bit start-address field of the low word changes
-    // (shared addresses < 256 KB never carry out of it).
-    if (lane == 0) {
+    // The whole warp runs the loop and its waits; one elected lane issues (the
+    // same lane every time, so its commits track its MMAs).  An MMA issue holds
+    // the thread for about the MMA's duration (64 cycles at M = N = 128), so
+    // the issuer is busy for most of each tile and every instruction between
+    // bursts delays the other tile.  Descriptors are precomputed; per MMA only
+    // the 14-bit start-address field of the low word changes (shared
+    // addresses < 256 KB never carry out of it).
+    {
       constexpr uint32_t ab = Elem<T>::kCode == TA_DTYPE_BF16 ? 1u : 0u;
       constexpr uint32_t idesc_s = instr_desc(ab, 0);
       constexpr uint32_t idesc_o = instr_desc(ab, 1);
@@ -309,9 +312,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < kDim / 16; ++k) {
           // 16 dims = 32 bytes along the swizzled K-major rows of Q and K
           const uint64_t off = ((k >> 2) * kHalfBytes + (k & 3) * 32) >> 4;
-          umma_ss(tmem + kColS + t * kKeys, qd + off, kd + off, idesc_s, k > 0 ? 1u : 0u);
+          umma_ss_warp(tmem + kColS + t * kKeys, qd + off, kd + off, idesc_s, k > 0 ? 1u : 0u);
         }
-        umma_commit(&bars[S_FULL + t]);
+        umma_commit_warp(&bars[S_FULL + t]);
       };
       auto issue_pv = [&](int t, int j) {  // O_t += P_t(j) V(j)
         const uint64_t vd = vdesc0 + uint64_t(j % kVStages) * (kTileBytes >> 4);
@@ -320,46 +323,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < kKeys / 16; ++k)
           // A = P in TMEM (16 keys = 8 packed columns); B = V, N-major: 16 keys
           // = two 8-row atoms = 2048 bytes; LBO = 64-column block stride.
-          umma_ts(tmem + kColO + t * kDim, p_tmem + k * 8, vd + ((k * 2048) >> 4), idesc_o,
+          umma_ts_warp(tmem + kColO + t * kDim, p_tmem + k * 8, vd + ((k * 2048) >> 4), idesc_o,
                   (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&bars[PV_DONE + t]);
+        // only the last P.V is waited for (the epilogue); an earlier one is
+        // known complete once the S issued after it is
+        if (j == ntiles - 1) umma_commit_warp(&bars[PV_DONE + t]);
       };
 
-      if (!mbar_wait(&bars[Q_FULL], 0, p.status)) alive = false;
-      if (alive && !mbar_wait(&bars[K_FULL], 0, p.status)) alive = false;
+      if (!warp_wait(&bars[Q_FULL], 0, p.status)) alive = false;
+      if (alive && !warp_wait(&bars[K_FULL], 0, p.status)) alive = false;
       if (alive) {
         tc_fence_after();
         issue_s(0, 0);
         if (ntile == 2) {
-          if (mbar_wait(&bars[Q_FULL + 1], 0, p.status)) {
+          if (warp_wait(&bars[Q_FULL + 1], 0, p.status)) {
             tc_fence_after();
             issue_s(1, 0);
           } else {
             alive = false;
           }
         }
-        umma_commit(&bars[K_EMPTY]);
+        umma_commit_warp(&bars[K_EMPTY]);
       }
       for (int j = 0; j < ntiles && alive; ++j) {
         const bool more = j + 1 < ntiles;
         const bool zeroed = tail && j == ntiles - 1;
         for (int t = 0; t < ntile; ++t) {
-          if (!mbar_wait(&bars[P_FULL + t], j & 1, p.status)) { alive = false; break; }
-          if (t == 0 && !mbar_wait(&bars[zeroed ? V_TAIL : V_FULL + j % kVStages],
+          if (!warp_wait(&bars[P_FULL + t], j & 1, p.status)) { alive = false; break; }
+          if (t == 0 && !warp_wait(&bars[zeroed ? V_TAIL : V_FULL + j % kVStages],
                                    zeroed ? 0 : (j / kVStages) & 1, p.status)) { alive = false; break; }
           tc_fence_after();
           issue_pv(t, j);
-          if (t == ntile - 1) umma_commit(&bars[V_EMPTY + j % kVStages]);
+          if (t == ntile - 1) umma_commit_warp(&bars[V_EMPTY + j % kVStages]);
           if (more) {
             if (t == 0) {
-              if (!mbar_wait(&bars[K_FULL + (j + 1) % kKStages], ((j + 1) / kKStages) & 1, p.status)) {
+              if (!warp_wait(&bars[K_FULL + (j + 1) % kKStages], ((j + 1) / kKStages) & 1, p.status)) {
                 alive = false;
                 break;
               }
               tc_fence_after();
             }
             issue_s(t, j + 1);
-            if (t == ntile - 1) umma_commit(&bars[K_EMPTY + (j + 1) % kKStages]);
+            if (t == ntile - 1) umma_commit_warp(&bars[K_EMPTY + (j + 1) % kKStages]);
           }
         }
       }
@@ -367,9 +372,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // is released: wait for the final release of each ring slot.
       if (alive) {
         for (int j = max(0, ntiles - kKStages); j < ntiles; ++j)
-          if (!mbar_wait(&bars[K_EMPTY + j % kKStages], (j / kKStages) & 1, p.status)) break;
+          if (!warp_wait(&bars[K_EMPTY + j % kKStages], (j / kKStages) & 1, p.status)) break;
         for (int j = max(0, ntiles - kVStages); j < ntiles; ++j)
-          if (!mbar_wait(&bars[V_EMPTY + j % kVStages], (j / kVStages) & 1, p.status)) break;
+          if (!warp_wait(&bars[V_EMPTY + j % kVStages], (j / kVStages) & 1, p.status)) break;
       }
     }
   } else if (warp >= kSoftmaxWarp0) {
@@ -484,9 +489,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       // epilogue: wait for the last P.V of this tile, then O / z and the LSE.
-      // Observing S_t(ntiles-1) implied P_t(ntiles-2) V done, so PV_DONE_t is
-      // at most one phase behind this wait.
-      if (alive && !warp_wait(&bars[PV_DONE + t], (ntiles - 1) & 1, p.status)) alive = false;
+      // PV_DONE_t completes once, with the last P.V of the tile.
+      if (alive && !warp_wait(&bars[PV_DONE + t], 0, p.status)) alive = false;
       tc_fence_after();
       const float inv = (alive && z > 0.f) ? 1.f / z : 0.f;
       float* dst = p.part + (head_rows + part_row0 + trow) * kDim;
