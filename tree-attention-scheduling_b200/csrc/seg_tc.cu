@@ -348,21 +348,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < ntiles && alive; ++j) {
         const bool more = j + 1 < ntiles;
         const bool zeroed = tail && j == ntiles - 1;
+        // V(j) and K(j+1) have normally landed well before tile A's P(j):
+        // wait for them first, so that P's arrival is followed by MMAs only.
+        if (!warp_wait(&bars[zeroed ? V_TAIL : V_FULL + j % kVStages], zeroed ? 0 : (j / kVStages) & 1, p.status) ||
+            (more && !warp_wait(&bars[K_FULL + (j + 1) % kKStages], ((j + 1) / kKStages) & 1, p.status))) {
+          alive = false;
+          break;
+        }
         for (int t = 0; t < ntile; ++t) {
           if (!warp_wait(&bars[P_FULL + t], j & 1, p.status)) { alive = false; break; }
-          if (t == 0 && !warp_wait(&bars[zeroed ? V_TAIL : V_FULL + j % kVStages],
-                                   zeroed ? 0 : (j / kVStages) & 1, p.status)) { alive = false; break; }
           tc_fence_after();
           issue_pv(t, j);
           if (t == ntile - 1) umma_commit_warp(&bars[V_EMPTY + j % kVStages]);
           if (more) {
-            if (t == 0) {
-              if (!warp_wait(&bars[K_FULL + (j + 1) % kKStages], ((j + 1) / kKStages) & 1, p.status)) {
-                alive = false;
-                break;
-              }
-              tc_fence_after();
-            }
             issue_s(t, j + 1);
             if (t == ntile - 1) umma_commit_warp(&bars[K_EMPTY + (j + 1) % kKStages]);
           }
