@@ -246,6 +246,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(qs + kHalfBytes, &tmap_q, 64, head * G, z, &bars[Q_FULL + t]);
         }
       }
+      // K(s) of the first round has landed -- K_FULL's first phase -- or has
+      // been consumed already -- K_EMPTY's first phase, should K_FULL have
+      // moved on (it cannot before K(s) is consumed, and K_EMPTY cannot move
+      // past its first phase before V(s) is loaded).
+      auto k_landed = [&](int s) {
+        const uint64_t start = global_ns();
+        while (!mbar_try_wait_for(&bars[K_FULL + s], 0, 100) && !mbar_test_wait(&bars[K_EMPTY + s], 0)) {
+          if (global_ns() - start > TA_WAIT_NS) {
+            set_status(p.status, TA_ERR_TIMEOUT);
+            return false;
+          }
+        }
+        return true;
+      };
       for (int j = 0; j < min(ntiles, kPrefetch); ++j) {
         tma_prefetch_l2(map, 0, int(k0) + j * kKeys, head);
         tma_prefetch_l2(map, 64, int(k0) + j * kKeys, head);
@@ -257,9 +271,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_prefetch_l2(map, 64, int(k0) + (j + kPrefetch) * kKeys, head);
         }
         if (j >= stages && !mbar_wait(&empty[st], ((j / stages) + 1) & 1, p.status)) break;
-        // the second stage waits until tile A's queries are in: the first
-        // tile's K and V and the queries share the start-up bandwidth alone
-        if (j == 1 && !mbar_wait(&bars[Q_FULL], 0, p.status)) break;
+        // Start-up order, the most needed first: the queries and K(0) (the
+        // first S), V(0) once K(0) has landed, K(1) once tile A's queries are
+        // in, V(1) once K(1) has landed.  All CTAs start together and share
+        // the HBM bandwidth, so a V tile requested early delays the first S.
+        if (is_k ? (j == 1 && !mbar_wait(&bars[Q_FULL], 0, p.status)) : (j < kKStages && !k_landed(j))) break;
         const int y = int(k0) + j * kKeys;
         unsigned char* dst = ring + st * kTileBytes;
         mbar_arrive_expect_tx(&full[st], kTileBytes);
