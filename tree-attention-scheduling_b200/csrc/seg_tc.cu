@@ -519,6 +519,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // and P.V MMAs have completed once P.V_t(last) has, so tile A reuses
         // the K ring and tile B the V ring.
         unsigned char* stage = smem + (t == 0 ? TcSmem::off_k : TcSmem::off_v);
+        // Each box leaves as soon as it is staged: the stores of all CTAs
+        // finish together and run at the L2 write rate, so starting them a
+        // box at a time overlaps them with the staging of the next boxes.
+        const int y = int(head_rows + part_row0 + t * kRows);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           unsigned char* box_row = stage + c * (kRows * 128) + row * 128;
@@ -527,16 +531,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<float4*>(box_row + ((i ^ (row & 7)) << 4)) =
                 make_float4(__uint_as_float(oa[c][4 * i]) * inv, __uint_as_float(oa[c][4 * i + 1]) * inv,
                             __uint_as_float(oa[c][4 * i + 2]) * inv, __uint_as_float(oa[c][4 * i + 3]) * inv);
+          fence_async_smem();
+          named_sync(1 + t, kSoftmaxWarps / 2 * 32);
+          if (quad == 0 && lane == 0) {
+            tma_store_2d(&tmap_part, stage + c * (kRows * 128), 32 * c, y);
+            bulk_commit_group();
+          }
         }
-        fence_async_smem();
-        named_sync(1 + t, kSoftmaxWarps / 2 * 32);
-        if (quad == 0 && lane == 0) {
-          const int y = int(head_rows + part_row0 + t * kRows);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tma_store_2d(&tmap_part, stage + c * (kRows * 128), 32 * c, y);
-          bulk_commit_group();
-          bulk_wait_read_all();               // shared memory must outlive the reads
-        }
+        if (quad == 0 && lane == 0) bulk_wait_read_all();   // shared memory must outlive the reads
       } else {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
