@@ -12,12 +12,12 @@
 //               L2 prefetch kPrefetch tiles ahead is off by default)
 //   warp 2      TMA producer of V tiles, likewise; it also zeroes the rows of
 //               the segment's last V tile that lie past the segment
-//   warp 1      one thread issues every tcgen05.mma: S_t = Q_t K^T (A = Q_t and
-//               B = K from shared memory) and O_t += P_t V (A = P_t from TMEM,
-//               written by softmax over its own S_t; B = V from shared memory),
-//               in the order S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) ...
-//               so the tensor pipe works on one tile while softmax works on the
-//               other
+//   warp 1      the MMA issuer, a converged warp whose elected lane issues every
+//               tcgen05.mma: S_t = Q_t K^T (A = Q_t and B = K from shared
+//               memory) and O_t += P_t V (A = P_t from TMEM, written by softmax
+//               over its own S_t; B = V from shared memory), in the order
+//               S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) ... so the
+//               tensor pipe works on one tile while softmax works on the other
 //   warps 3-6   softmax of tile A, warps 7-10 of tile B (a warp reaches the
 //               TMEM lane quadrant warp % 4): one thread per query
 //               row (TMEM lane) holding the row's 128 scores, so row maxima and
