@@ -609,10 +609,14 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
         }
         return false;
       };
-      // Trail: copy and release every slot up to the next task with tiles.
-      // Only called for slots the lead has already waited for.
+      // Trail: copy and release every slot up to the next task with tiles,
+      // never past the lead (only slots the lead has waited for).  It runs on
+      // every pass, not only while a P.V is outstanding: slots of tasks without
+      // tiles must be released even when no S is in flight, since the scheduler
+      // needs them to publish the tasks 8 places later, which the lead may be
+      // waiting for.
       auto trail_settle = [&]() {
-        while (pc.k < count && !p_loaded) {
+        while (pc.k < count && !p_loaded && (pc.k < sc.k || (pc.k == sc.k && s_loaded))) {
           pc.t = load_task(slot_of(pc.k));
           mbar_arrive(&task_empty[pc.k % kTQ]);
           if (pc.t.nseg > 0 && pc.t.ntiles > 0) {
@@ -625,6 +629,7 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
       uint64_t idle_since = 0;
       while (alive) {
         bool did = false;
+        if (!p_loaded) trail_settle();
         if (pc.g < sc.g) {                              // P.V of the oldest tile whose S is issued
           if (!p_loaded) trail_settle();
           const int st = pc.g % S;
@@ -761,13 +766,28 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
     int qi = 0;           // index among tasks with tiles
     int pend_k = -1, pend_g = 0;   // task whose epilogue is deferred past the next task's first tile
     float m[R];           // agreed row maxima of the current task (identical in every thread)
-    for (int k = 0; k < count; ++k) {
-      const bool t_ok = alive && warp_wait(&task_full[k % kTQ], (k / kTQ) & 1, p.status);
-      if (named_sync_or(1, kSoftmaxThreads, !t_ok)) alive = false;
-      if (!alive) break;
-      const TaskR t = load_task(slot_of(k));
+    // One pass past the end of the list (k == count) runs the last pending
+    // epilogue at the same call site as a task without tiles does.
+    for (int k = 0; k <= count; ++k) {
+      const bool end = k == count;
+      if (!end) {
+        const bool t_ok = alive && warp_wait(&task_full[k % kTQ], (k / kTQ) & 1, p.status);
+        if (named_sync_or(1, kSoftmaxThreads, !t_ok)) alive = false;
+      }
+      TaskR t = {};
+      if (!end && alive) t = load_task(slot_of(k));
       const int ntiles = t.ntiles, rows = t.rows, flags = t.flags;
       if ((flags & TASK_BAD) && kk == 0) set_status(p.status, TA_ERR_BOUNDS);
+      if ((end || !alive || !(flags & TASK_WRITE) || ntiles == 0) && pend_k >= 0) {
+        // A task without tiles has nothing to overlap with the pending
+        // epilogue, so run it now: the pending task's slot must be released
+        // before the scheduler can publish the task 8 places after it, and a
+        // list may hold 7 or more tasks without tiles in a row (empty decode
+        // tails) -- waiting for the next task with tiles would stall.
+        epilogue(pend_k, pend_g, (qi - 1) & 1);
+        pend_k = -1;
+      }
+      if (end || !alive) break;
       if (!(flags & TASK_WRITE)) {
         release(k);
         continue;
@@ -979,7 +999,6 @@ __global__ void __launch_bounds__(kThreads, KnCfg<R>::kCtasPerSm)
       pend_g = g - 1;
       ++qi;
     }
-    if (pend_k >= 0) epilogue(pend_k, pend_g, (qi - 1) & 1);
   }
 
   // Every warp reconverges (roles ran on one lane) before the CTA-wide barrier.
