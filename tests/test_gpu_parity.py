@@ -180,6 +180,29 @@ def test_cached_decode_plan_matches_oracle():
         check_against_oracle(q, k, v, paths, out, lse.cpu())
 
 
+def test_cached_decode_plan_with_long_runs_of_empty_tails():
+    """1200 requests with private leaves and a cached decode plan: before the first token every tail is
+    empty, and some keys-in-lanes CTAs run 8 or more tasks without tiles in a row after a task with tiles
+    (the task ring is 8 slots deep).  The step completes with status OK and matches the oracle, then again
+    with one token per tail."""
+    nreq, steps = 1200, 2
+    base = KVTree.synthetic([-1] + [0] * nreq, [512] + [16] * nreq, list(range(1, nreq + 1)))
+    prefix = base.storage_tokens
+    q, k, v = make_inputs(nreq, prefix + nreq * steps, 32, 8, 128, torch.bfloat16, seed=303)
+    qd = q.cuda()
+    kp, vp = pack_kv(k.cuda(), v.cuda())
+    cached = CachedDecodePlan(schedule(base, 32, 8, 128, "cube", CostModel.b200()), qd, prefix, steps)
+    sample = list(range(0, nreq, 97)) + [nreq - 1]
+    for n in (0, 1):
+        p = cached.update(n)
+        lse = torch.empty(nreq, 32, device="cuda")
+        out = attention_matrix(qd, kp, vp, p, out_lse=lse).cpu()
+        torch.cuda.synchronize()
+        check_status(p)
+        paths = [base.paths[r] + tuple(prefix + r * steps + t for t in range(n)) for r in sample]
+        check_against_oracle(q[sample], k, v, paths, out[sample], lse.cpu()[sample])
+
+
 def test_graph_capture_replays_same_result():
     tree = build_tree(_Lib, SPECS["small_config1"])
     q, k, v = make_inputs(8, tree.storage_tokens, 32, 8, 128, torch.bfloat16, seed=3)

@@ -359,3 +359,31 @@ def test_keys_in_lanes_barrier_protocol(stages, qbufs, shape):
         cta = Cta(tasks, stages, qbufs, rng)
         cta.run()
         assert len(cta.epi_done) == sum(1 for t in tasks if t > 0)
+
+
+def test_large_decode_batch_has_long_runs_of_tasks_without_tiles():
+    """The stall the model found is reachable: a cached decode plan for 1200 requests puts, in some
+    keys-in-lanes CTA's list, 8 or more growing tails in a row after a task with tiles -- at the step
+    where the tails are still empty every one of them is a task without tiles."""
+    import numpy as np
+    from tree_attention import CostModel, KVTree, kernels, schedule
+    from tree_attention.schedule import Job, physical_jobs
+    nreq, steps = 1200, 2
+    tree = KVTree.synthetic([-1] + [0] * nreq, [512] + [16] * nreq, list(range(1, nreq + 1)))
+    plan = schedule(tree, 32, 8, 128, "cube", CostModel.b200())
+    prefix = tree.storage_tokens
+    tails = [Job((r,), tuple(range(prefix + r * steps, prefix + (r + 1) * steps))) for r in range(nreq)]
+    jobs = physical_jobs(plan.jobs + tails)
+    jobs.sort(key=lambda job: len(job.requests) * 4 > 16)
+    meta = kernels.build_metadata(jobs, nreq, 4, True, heads=8, sms=148, no_split_from=prefix)
+    offsets, tasks, segs = (np.asarray(meta[key]) for key in ("kn_offsets", "kn_tasks", "kn_segs"))
+    growing = ((segs[:, 7] >> 30) & 1).astype(bool)
+    empty = np.array([growing[t[0]:t[0] + t[1]].all() for t in tasks])
+    longest = 0
+    for c in range(len(offsets) - 1):
+        run, seen_tiles = 0, False
+        for e in empty[offsets[c]:offsets[c + 1]]:
+            run = run + 1 if (e and seen_tiles) else 0
+            seen_tiles |= not e
+            longest = max(longest, run)
+    assert longest >= 8
